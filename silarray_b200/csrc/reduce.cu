@@ -1,0 +1,623 @@
+// Reductions: whole-array sum/min/max/argmax, row-wise softmax / layer_norm /
+// argmax, and sum over an axis.  All HBM-bound; each input byte is read once.
+//
+// Whole-array reductions use a fixed grid (a multiple of the SM count) whose
+// CTAs write one partial each into the caller's workspace, then a one-CTA
+// finish kernel combines the partials in index order, so results are
+// deterministic for a given GPU.
+//
+// Row ops keep the whole row on chip: each thread holds VPT float4 of the
+// row in registers, so softmax and layer_norm read HBM once and write once
+// (the reference reads the row 2-3 times: include/gpu_kernels.metal:1316-1467).
+#include <float.h>
+
+#include "common.cuh"
+
+namespace silcu {
+namespace {
+
+// ------------------------------------------------------------- block reduce
+template <int NT, typename T, typename F>
+__device__ __forceinline__ T block_reduce(T v, T *smem, F op) {
+  constexpr int NW = NT / 32;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if (NW == 1) return v;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (lane == 0) smem[w] = v;
+  __syncthreads();
+  T r = smem[0];
+#pragma unroll
+  for (int i = 1; i < NW; i++) r = op(r, smem[i]);  // broadcast reads, fixed order
+  __syncthreads();  // smem is reused by the next reduction
+  return r;
+}
+
+struct Add {
+  template <typename T>
+  __device__ T operator()(T a, T b) const { return a + b; }
+};
+struct Max {
+  __device__ float operator()(float a, float b) const { return fmaxf(a, b); }
+  __device__ unsigned long long operator()(unsigned long long a, unsigned long long b) const {
+    return a > b ? a : b;
+  }
+};
+
+// Orderable encoding of a float: unsigned compare == float compare.
+__device__ __forceinline__ uint32_t ord(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float unord(uint32_t u) {
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
+}
+// Argmax key: larger value wins, then the smaller index.  Only values above
+// FLT_MIN are candidates (include/array.h:1733-1740 starts its running max at
+// numeric_limits<float>::min() and compares with a strict '>'); NaN never is.
+__device__ __forceinline__ unsigned long long amax_key(float v, uint64_t idx) {
+  if (!(v > FLT_MIN)) return 0ull;
+  return (uint64_t(ord(v)) << 32) | uint64_t(0xFFFFFFFFu - uint32_t(idx));
+}
+
+// ---------------------------------------------------- whole-array reductions
+constexpr int kRedThreads = 512;
+constexpr int kRedCtasPerSm = 4;
+constexpr int kMaxPartials = 4096;
+
+enum RedKind { kSum = 0, kMinK = 1, kMaxK = 2, kSumI = 3, kArgmax = 4 };
+
+template <int KIND>
+struct RedT;
+template <> struct RedT<kSum> { using T = double; };
+template <> struct RedT<kMinK> { using T = float; };
+template <> struct RedT<kMaxK> { using T = float; };
+template <> struct RedT<kSumI> { using T = uint32_t; };
+template <> struct RedT<kArgmax> { using T = unsigned long long; };
+
+template <int KIND>
+__device__ __forceinline__ typename RedT<KIND>::T red_identity() {
+  if (KIND == kMinK) return __int_as_float(0x7f800000);   // +inf
+  if (KIND == kMaxK) return __int_as_float(0xff800000);   // -inf
+  return 0;
+}
+
+template <int KIND, typename T>
+__device__ __forceinline__ T red_op(T a, T b) {
+  if (KIND == kMinK) return fminf(a, b);
+  if (KIND == kMaxK) return fmaxf(a, b);
+  if (KIND == kArgmax) return a > b ? a : b;
+  return a + b;
+}
+
+template <int KIND, typename In>
+__device__ __forceinline__ typename RedT<KIND>::T red_elem(In v, uint64_t idx) {
+  if (KIND == kSum) return double(v);
+  if (KIND == kSumI) return uint32_t(v);
+  if (KIND == kArgmax) return amax_key(float(v), idx);
+  return float(v);
+}
+
+template <int KIND, typename In>
+__global__ void __launch_bounds__(kRedThreads) reduce_partials(const In *__restrict__ in, uint64_t n,
+                                                               typename RedT<KIND>::T *__restrict__ part) {
+  using T = typename RedT<KIND>::T;
+  __shared__ T smem[kRedThreads / 32];
+  T acc = red_identity<KIND>();
+  const uint64_t tid = uint64_t(blockIdx.x) * kRedThreads + threadIdx.x;
+  const uint64_t nthreads = uint64_t(gridDim.x) * kRedThreads;
+  const bool vec = (reinterpret_cast<uintptr_t>(in) & 15) == 0;
+  const uint64_t n4 = vec ? n / 4 : 0;
+  // 4 independent 16-byte loads in flight per thread per iteration.
+  uint64_t i = tid;
+  for (; i + 3 * nthreads < n4; i += 4 * nthreads) {
+    float4 f[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) f[u] = __ldcs(reinterpret_cast<const float4 *>(in) + i + u * nthreads);
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const In *e = reinterpret_cast<const In *>(&f[u]);
+      const uint64_t base = (i + u * nthreads) * 4;
+#pragma unroll
+      for (int k = 0; k < 4; k++) acc = red_op<KIND>(acc, red_elem<KIND>(e[k], base + k));
+    }
+  }
+  for (; i < n4; i += nthreads) {
+    float4 f = __ldcs(reinterpret_cast<const float4 *>(in) + i);
+    const In *e = reinterpret_cast<const In *>(&f);
+#pragma unroll
+    for (int k = 0; k < 4; k++) acc = red_op<KIND>(acc, red_elem<KIND>(e[k], i * 4 + k));
+  }
+  for (uint64_t j = n4 * 4 + tid; j < n; j += nthreads) acc = red_op<KIND>(acc, red_elem<KIND>(in[j], j));
+  // block reduce
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc = red_op<KIND>(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (lane == 0) smem[w] = acc;
+  __syncthreads();
+  if (w == 0) {
+    T r = lane < kRedThreads / 32 ? smem[lane] : red_identity<KIND>();
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) r = red_op<KIND>(r, __shfl_xor_sync(0xffffffffu, r, o));
+    if (lane == 0) part[blockIdx.x] = r;
+  }
+}
+
+template <int KIND, typename Out>
+__global__ void __launch_bounds__(1024) reduce_finish(const typename RedT<KIND>::T *__restrict__ part,
+                                                      int nparts, Out *__restrict__ out,
+                                                      float *__restrict__ out_value,
+                                                      const float *__restrict__ in) {
+  using T = typename RedT<KIND>::T;
+  __shared__ T smem[32];
+  T acc = red_identity<KIND>();
+  for (int i = threadIdx.x; i < nparts; i += 1024) acc = red_op<KIND>(acc, part[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc = red_op<KIND>(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (lane == 0) smem[w] = acc;
+  __syncthreads();
+  if (w == 0) {
+    T r = smem[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) r = red_op<KIND>(r, __shfl_xor_sync(0xffffffffu, r, o));
+    if (lane == 0) {
+      if (KIND == kSum) {
+        *reinterpret_cast<float *>(out) = float(r);
+      } else if (KIND == kArgmax) {
+        const unsigned long long key = (unsigned long long)r;
+        const int64_t idx = key ? int64_t(0xFFFFFFFFu - uint32_t(key & 0xFFFFFFFFu)) : 0;
+        *reinterpret_cast<int64_t *>(out) = idx;
+        if (out_value) *out_value = key ? unord(uint32_t(key >> 32)) : in[0];
+      } else {
+        *out = Out(r);
+      }
+    }
+  }
+}
+
+int red_grid(uint64_t n) {
+  uint64_t want = (n + kRedThreads * 16 - 1) / (kRedThreads * 16);
+  uint64_t cap = uint64_t(sm_count()) * kRedCtasPerSm;
+  if (want > cap) want = cap;
+  if (want < 1) want = 1;
+  if (want > kMaxPartials) want = kMaxPartials;
+  return int(want);
+}
+
+template <int KIND, typename In, typename Out>
+silcu_status run_reduce(const char *name, const In *in, size_t n, Out *out, float *out_value,
+                        void *ws, size_t ws_bytes, silcu_stream stream) {
+  using T = typename RedT<KIND>::T;
+  if (!in || !out) return fail(SILCU_INVALID_ARGUMENT, "%s: null pointer", name);
+  if (n == 0) return fail(SILCU_INVALID_ARGUMENT, "%s: empty input", name);
+  if (KIND == kArgmax && n > 0xFFFFFFFFull) return fail(SILCU_UNSUPPORTED, "%s: n >= 2^32", name);
+  const int g = red_grid(n);
+  if (!ws || ws_bytes < size_t(g) * sizeof(T))
+    return fail(SILCU_WORKSPACE_TOO_SMALL, "%s: workspace %zu < %zu", name, ws_bytes, size_t(g) * sizeof(T));
+  T *part = static_cast<T *>(ws);
+  cudaStream_t s = as_stream(stream);
+  reduce_partials<KIND, In><<<g, kRedThreads, 0, s>>>(in, n, part);
+  reduce_finish<KIND, Out><<<1, 1024, 0, s>>>(part, g, out, out_value, reinterpret_cast<const float *>(in));
+  return check_launch(name);
+}
+
+// ------------------------------------------------------------------ row ops
+enum RowOp { kSoftmax = 0, kLayerNorm = 1, kRowArgmax = 2 };
+
+struct RowArgs {
+  const float *in;
+  float *out;
+  int32_t *idx;
+  const float *gamma, *beta;
+  uint32_t rows, cols;
+  float eps;
+};
+
+// One CTA per row, the row cached in registers: VPT float4 per thread.
+// Requires cols % 4 == 0 and 16-byte aligned rows; cols <= NT * VPT * 4.
+template <int OP, int NT, int VPT>
+__global__ void __launch_bounds__(NT) row_kernel(const RowArgs a) {
+  __shared__ float sf[NT / 32];
+  __shared__ unsigned long long sk[NT / 32];
+  const uint32_t c4 = a.cols / 4;
+  const int t = threadIdx.x;
+  for (uint32_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const float4 *src = reinterpret_cast<const float4 *>(a.in + size_t(row) * a.cols);
+    float4 v[VPT];
+#pragma unroll
+    for (int j = 0; j < VPT; j++) {
+      const uint32_t c = t + j * NT;
+      v[j] = c < c4 ? __ldcs(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (OP == kSoftmax) {
+      float m = __int_as_float(0xff800000);
+#pragma unroll
+      for (int j = 0; j < VPT; j++)
+        if (t + j * NT < c4) m = fmaxf(m, fmaxf(fmaxf(v[j].x, v[j].y), fmaxf(v[j].z, v[j].w)));
+      m = block_reduce<NT>(m, sf, Max());
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < VPT; j++) {
+        if (t + j * NT < c4) {
+          v[j].x = expf(__fsub_rn(v[j].x, m));
+          v[j].y = expf(__fsub_rn(v[j].y, m));
+          v[j].z = expf(__fsub_rn(v[j].z, m));
+          v[j].w = expf(__fsub_rn(v[j].w, m));
+          s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+        }
+      }
+      s = block_reduce<NT>(s, sf, Add());
+      const float inv = __frcp_rn(s);
+      float4 *dst = reinterpret_cast<float4 *>(a.out + size_t(row) * a.cols);
+#pragma unroll
+      for (int j = 0; j < VPT; j++) {
+        const uint32_t c = t + j * NT;
+        if (c < c4)
+          __stcs(dst + c, make_float4(__fmul_rn(v[j].x, inv), __fmul_rn(v[j].y, inv),
+                                      __fmul_rn(v[j].z, inv), __fmul_rn(v[j].w, inv)));
+      }
+    } else if (OP == kLayerNorm) {
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < VPT; j++) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+      s = block_reduce<NT>(s, sf, Add());
+      const float mu = __fdiv_rn(s, float(a.cols));
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < VPT; j++) {
+        if (t + j * NT < c4) {
+          v[j].x = __fsub_rn(v[j].x, mu);
+          v[j].y = __fsub_rn(v[j].y, mu);
+          v[j].z = __fsub_rn(v[j].z, mu);
+          v[j].w = __fsub_rn(v[j].w, mu);
+          ss += (__fmul_rn(v[j].x, v[j].x) + __fmul_rn(v[j].y, v[j].y)) +
+                (__fmul_rn(v[j].z, v[j].z) + __fmul_rn(v[j].w, v[j].w));
+        }
+      }
+      ss = block_reduce<NT>(ss, sf, Add());
+      const float inv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(a.cols)), a.eps)));
+      float4 *dst = reinterpret_cast<float4 *>(a.out + size_t(row) * a.cols);
+      const float4 *g4 = reinterpret_cast<const float4 *>(a.gamma);
+      const float4 *b4 = reinterpret_cast<const float4 *>(a.beta);
+#pragma unroll
+      for (int j = 0; j < VPT; j++) {
+        const uint32_t c = t + j * NT;
+        if (c < c4) {
+          const float4 g = __ldg(g4 + c), b = __ldg(b4 + c);
+          float4 o;
+          o.x = __fadd_rn(__fmul_rn(__fmul_rn(v[j].x, inv), g.x), b.x);
+          o.y = __fadd_rn(__fmul_rn(__fmul_rn(v[j].y, inv), g.y), b.y);
+          o.z = __fadd_rn(__fmul_rn(__fmul_rn(v[j].z, inv), g.z), b.z);
+          o.w = __fadd_rn(__fmul_rn(__fmul_rn(v[j].w, inv), g.w), b.w);
+          __stcs(dst + c, o);
+        }
+      }
+    } else {  // argmax
+      unsigned long long best = 0ull;
+#pragma unroll
+      for (int j = 0; j < VPT; j++) {
+        const uint32_t c = t + j * NT;
+        if (c < c4) {
+          const uint32_t base = c * 4;
+          unsigned long long k0 = amax_key(v[j].x, base), k1 = amax_key(v[j].y, base + 1);
+          unsigned long long k2 = amax_key(v[j].z, base + 2), k3 = amax_key(v[j].w, base + 3);
+          k0 = k0 > k1 ? k0 : k1;
+          k2 = k2 > k3 ? k2 : k3;
+          k0 = k0 > k2 ? k0 : k2;
+          best = best > k0 ? best : k0;
+        }
+      }
+      best = block_reduce<NT>(best, sk, Max());
+      if (t == 0) a.idx[row] = best ? int32_t(0xFFFFFFFFu - uint32_t(best & 0xFFFFFFFFu)) : 0;
+    }
+  }
+}
+
+// Generic fallback: any cols (no alignment requirement), re-reads the row
+// from global memory (the second read hits L2 for rows up to a few MB).
+template <int OP>
+__global__ void __launch_bounds__(512) row_kernel_generic(const RowArgs a) {
+  constexpr int NT = 512;
+  __shared__ float sf[NT / 32];
+  __shared__ unsigned long long sk[NT / 32];
+  const int t = threadIdx.x;
+  for (uint32_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const float *src = a.in + size_t(row) * a.cols;
+    float *dst = a.out ? a.out + size_t(row) * a.cols : nullptr;
+    if (OP == kSoftmax) {
+      float m = __int_as_float(0xff800000);
+      for (uint32_t c = t; c < a.cols; c += NT) m = fmaxf(m, src[c]);
+      m = block_reduce<NT>(m, sf, Max());
+      float s = 0.f;
+      for (uint32_t c = t; c < a.cols; c += NT) s += expf(__fsub_rn(src[c], m));
+      s = block_reduce<NT>(s, sf, Add());
+      const float inv = __frcp_rn(s);
+      for (uint32_t c = t; c < a.cols; c += NT) dst[c] = __fmul_rn(expf(__fsub_rn(src[c], m)), inv);
+    } else if (OP == kLayerNorm) {
+      float s = 0.f;
+      for (uint32_t c = t; c < a.cols; c += NT) s += src[c];
+      s = block_reduce<NT>(s, sf, Add());
+      const float mu = __fdiv_rn(s, float(a.cols));
+      float ss = 0.f;
+      for (uint32_t c = t; c < a.cols; c += NT) {
+        const float d = __fsub_rn(src[c], mu);
+        ss += __fmul_rn(d, d);
+      }
+      ss = block_reduce<NT>(ss, sf, Add());
+      const float inv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(a.cols)), a.eps)));
+      for (uint32_t c = t; c < a.cols; c += NT)
+        dst[c] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(src[c], mu), inv), a.gamma[c]), a.beta[c]);
+    } else {
+      unsigned long long best = 0ull;
+      for (uint32_t c = t; c < a.cols; c += NT) {
+        const unsigned long long k = amax_key(src[c], c);
+        best = best > k ? best : k;
+      }
+      best = block_reduce<NT>(best, sk, Max());
+      if (t == 0) a.idx[row] = best ? int32_t(0xFFFFFFFFu - uint32_t(best & 0xFFFFFFFFu)) : 0;
+    }
+  }
+}
+
+template <int OP, int NT, int VPT>
+void launch_row(const RowArgs &a, cudaStream_t s) {
+  uint32_t g = a.rows;
+  row_kernel<OP, NT, VPT><<<g, NT, 0, s>>>(a);
+}
+
+template <int OP>
+silcu_status run_rows(const char *name, const RowArgs &a, silcu_stream stream) {
+  if (a.rows == 0 || a.cols == 0) return SILCU_OK;
+  cudaStream_t s = as_stream(stream);
+  const bool vec = (a.cols % 4 == 0) && aligned16(a.in) && (!a.out || aligned16(a.out)) &&
+                   (OP != kLayerNorm || (aligned16(a.gamma) && aligned16(a.beta)));
+  const uint32_t c = a.cols;
+  if (vec && c <= 128) launch_row<OP, 32, 1>(a, s);
+  else if (vec && c <= 512) launch_row<OP, 64, 2>(a, s);
+  else if (vec && c <= 1024) launch_row<OP, 128, 2>(a, s);
+  else if (vec && c <= 2048) launch_row<OP, 256, 2>(a, s);
+  else if (vec && c <= 4096) launch_row<OP, 256, 4>(a, s);
+  else if (vec && c <= 8192) launch_row<OP, 512, 4>(a, s);
+  else if (vec && c <= 16384) launch_row<OP, 512, 8>(a, s);
+  else if (vec && c <= 32768) launch_row<OP, 1024, 8>(a, s);
+  else row_kernel_generic<OP><<<a.rows < 65535u * 16 ? a.rows : 65535u * 16, 512, 0, s>>>(a);
+  return check_launch(name);
+}
+
+// ------------------------------------------- split-row argmax (few long rows)
+__global__ void __launch_bounds__(512) argmax_split_partials(const float *__restrict__ in, uint64_t cols,
+                                                             uint32_t splits, unsigned long long *part) {
+  __shared__ unsigned long long sk[16];
+  const uint32_t row = blockIdx.y, sp = blockIdx.x;
+  const uint64_t chunk = (cols + splits - 1) / splits;
+  const uint64_t c0 = sp * chunk, c1 = c0 + chunk < cols ? c0 + chunk : cols;
+  const float *src = in + uint64_t(row) * cols;
+  unsigned long long best = 0ull;
+  for (uint64_t c = c0 + threadIdx.x; c < c1; c += 512) {
+    const unsigned long long k = amax_key(__ldcs(src + c), c);
+    best = best > k ? best : k;
+  }
+  best = block_reduce<512>(best, sk, Max());
+  if (threadIdx.x == 0) part[uint64_t(row) * splits + sp] = best;
+}
+
+__global__ void argmax_split_finish(const unsigned long long *part, uint32_t rows, uint32_t splits,
+                                    int32_t *out) {
+  const uint32_t row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  unsigned long long best = 0ull;
+  for (uint32_t s = 0; s < splits; s++) {
+    const unsigned long long k = part[uint64_t(row) * splits + s];
+    best = best > k ? best : k;
+  }
+  out[row] = best ? int32_t(0xFFFFFFFFu - uint32_t(best & 0xFFFFFFFFu)) : 0;
+}
+
+uint32_t argmax_splits(size_t rows, size_t cols) {
+  const size_t target = size_t(sm_count()) * 8;
+  if (rows >= target || cols < 8192) return 1;
+  size_t s = (target + rows - 1) / rows;
+  const size_t max_s = cols / 4096;
+  if (s > max_s) s = max_s;
+  if (s < 1) s = 1;
+  if (s > 65535) s = 65535;
+  return uint32_t(s);
+}
+
+// ------------------------------------------------------------- sum over axis
+// Rows (inner == 1): one warp per row for short rows, else one CTA per row.
+__global__ void __launch_bounds__(256) sum_rows_kernel(const float *__restrict__ in, float *__restrict__ out,
+                                                       uint64_t rows, uint64_t cols, bool vec) {
+  __shared__ float sf[8];
+  for (uint64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float *src = in + row * cols;
+    float s = 0.f;
+    if (vec) {
+      const float4 *s4 = reinterpret_cast<const float4 *>(src);
+      for (uint64_t c = threadIdx.x; c < cols / 4; c += 256) {
+        const float4 f = __ldcs(s4 + c);
+        s += (f.x + f.y) + (f.z + f.w);
+      }
+    } else {
+      for (uint64_t c = threadIdx.x; c < cols; c += 256) s += src[c];
+    }
+    s = block_reduce<256>(s, sf, Add());
+    if (threadIdx.x == 0) out[row] = s;
+  }
+}
+
+__global__ void __launch_bounds__(256) sum_rows_warp_kernel(const float *__restrict__ in,
+                                                            float *__restrict__ out, uint64_t rows,
+                                                            uint64_t cols) {
+  const uint64_t warp = (uint64_t(blockIdx.x) * 256 + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const float *src = in + warp * cols;
+  float s = 0.f;
+  for (uint64_t c = lane; c < cols; c += 32) s += src[c];
+  s = warp_sum(s);
+  if (lane == 0) out[warp] = s;
+}
+
+// Columns (inner > 1): thread per inner index, rows of the axis split into
+// `splits` chunks whose partials land in the workspace; a second pass adds
+// the chunks in order.
+__global__ void __launch_bounds__(256) sum_cols_kernel(const float *__restrict__ in, float *__restrict__ dst,
+                                                       uint64_t outer, uint64_t len, uint64_t inner,
+                                                       uint32_t splits) {
+  const uint64_t i = uint64_t(blockIdx.x) * 256 + threadIdx.x;
+  const uint64_t o = blockIdx.y;
+  const uint32_t sp = blockIdx.z;
+  if (i >= inner) return;
+  const uint64_t chunk = (len + splits - 1) / splits;
+  const uint64_t k0 = sp * chunk, k1 = k0 + chunk < len ? k0 + chunk : len;
+  const float *src = in + o * len * inner + i;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  uint64_t k = k0;
+  for (; k + 4 <= k1; k += 4) {
+    s0 += __ldcs(src + (k + 0) * inner);
+    s1 += __ldcs(src + (k + 1) * inner);
+    s2 += __ldcs(src + (k + 2) * inner);
+    s3 += __ldcs(src + (k + 3) * inner);
+  }
+  for (; k < k1; k++) s0 += __ldcs(src + k * inner);
+  dst[(uint64_t(sp) * outer + o) * inner + i] = (s0 + s1) + (s2 + s3);
+}
+
+__global__ void __launch_bounds__(256) sum_cols_finish(const float *__restrict__ part, float *__restrict__ out,
+                                                       uint64_t total, uint32_t splits) {
+  const uint64_t j = uint64_t(blockIdx.x) * 256 + threadIdx.x;
+  if (j >= total) return;
+  float s = 0.f;
+  for (uint32_t sp = 0; sp < splits; sp++) s += part[uint64_t(sp) * total + j];
+  out[j] = s;
+}
+
+uint32_t col_splits(size_t outer, size_t len, size_t inner) {
+  const size_t blocks = ((inner + 255) / 256) * outer;
+  const size_t target = size_t(sm_count()) * 8;
+  if (blocks >= target) return 1;
+  size_t s = (target + blocks - 1) / blocks;
+  const size_t max_s = len / 16 > 0 ? len / 16 : 1;
+  if (s > max_s) s = max_s;
+  if (s > 65535) s = 65535;
+  return uint32_t(s < 1 ? 1 : s);
+}
+
+}  // namespace
+}  // namespace silcu
+
+using namespace silcu;
+
+extern "C" {
+
+size_t silcu_reduce_workspace_bytes(size_t n) {
+  (void)n;
+  return size_t(kMaxPartials) * 8;
+}
+
+silcu_status silcu_sum_f32(const float *in, size_t n, float *out, void *ws, size_t wsb, silcu_stream s) {
+  return run_reduce<kSum, float, float>("sum_f32", in, n, out, nullptr, ws, wsb, s);
+}
+silcu_status silcu_min_f32(const float *in, size_t n, float *out, void *ws, size_t wsb, silcu_stream s) {
+  return run_reduce<kMinK, float, float>("min_f32", in, n, out, nullptr, ws, wsb, s);
+}
+silcu_status silcu_max_f32(const float *in, size_t n, float *out, void *ws, size_t wsb, silcu_stream s) {
+  return run_reduce<kMaxK, float, float>("max_f32", in, n, out, nullptr, ws, wsb, s);
+}
+silcu_status silcu_sum_i32(const int32_t *in, size_t n, int32_t *out, void *ws, size_t wsb, silcu_stream s) {
+  return run_reduce<kSumI, int32_t, int32_t>("sum_i32", in, n, out, nullptr, ws, wsb, s);
+}
+silcu_status silcu_argmax_all_f32(const float *in, size_t n, int64_t *out_index, float *out_value, void *ws,
+                                  size_t wsb, silcu_stream s) {
+  return run_reduce<kArgmax, float, int64_t>("argmax_all_f32", in, n, out_index, out_value, ws, wsb, s);
+}
+
+silcu_status silcu_softmax_f32(const float *in, float *out, size_t rows, size_t cols, silcu_stream s) {
+  if (rows && cols && (!in || !out)) return fail(SILCU_INVALID_ARGUMENT, "softmax: null pointer");
+  if (rows > 0xFFFFFFFFull || cols > 0xFFFFFFFFull) return fail(SILCU_UNSUPPORTED, "softmax: dims >= 2^32");
+  RowArgs a{in, out, nullptr, nullptr, nullptr, uint32_t(rows), uint32_t(cols), 0.f};
+  return run_rows<kSoftmax>("softmax", a, s);
+}
+
+silcu_status silcu_layer_norm_f32(const float *in, float *out, const float *gamma, const float *beta,
+                                  size_t rows, size_t cols, float eps, silcu_stream s) {
+  if (rows && cols && (!in || !out || !gamma || !beta))
+    return fail(SILCU_INVALID_ARGUMENT, "layer_norm: null pointer");
+  if (rows > 0xFFFFFFFFull || cols > 0xFFFFFFFFull) return fail(SILCU_UNSUPPORTED, "layer_norm: dims >= 2^32");
+  RowArgs a{in, out, nullptr, gamma, beta, uint32_t(rows), uint32_t(cols), eps};
+  return run_rows<kLayerNorm>("layer_norm", a, s);
+}
+
+size_t silcu_argmax_workspace_bytes(size_t rows, size_t cols) {
+  const uint32_t sp = argmax_splits(rows, cols);
+  return sp > 1 ? rows * sp * sizeof(unsigned long long) : 0;
+}
+
+silcu_status silcu_argmax_f32(const float *in, int32_t *out, size_t rows, size_t cols, void *ws, size_t wsb,
+                              silcu_stream stream) {
+  if (rows == 0) return SILCU_OK;
+  if (!in || !out) return fail(SILCU_INVALID_ARGUMENT, "argmax: null pointer");
+  if (cols == 0) return fail(SILCU_INVALID_ARGUMENT, "argmax: empty rows");
+  if (rows > 65535u || cols > 0xFFFFFFFFull) {
+    if (rows > 0xFFFFFFFFull || cols > 0xFFFFFFFFull) return fail(SILCU_UNSUPPORTED, "argmax: dims >= 2^32");
+  }
+  const uint32_t sp = argmax_splits(rows, cols);
+  if (sp > 1) {
+    const size_t need = rows * sp * sizeof(unsigned long long);
+    if (!ws || wsb < need) return fail(SILCU_WORKSPACE_TOO_SMALL, "argmax: workspace %zu < %zu", wsb, need);
+    cudaStream_t s = as_stream(stream);
+    argmax_split_partials<<<dim3(sp, uint32_t(rows)), 512, 0, s>>>(in, cols, sp,
+                                                                   static_cast<unsigned long long *>(ws));
+    argmax_split_finish<<<uint32_t((rows + 255) / 256), 256, 0, s>>>(
+        static_cast<const unsigned long long *>(ws), uint32_t(rows), sp, out);
+    return check_launch("argmax(split)");
+  }
+  RowArgs a{in, nullptr, out, nullptr, nullptr, uint32_t(rows), uint32_t(cols), 0.f};
+  return run_rows<kRowArgmax>("argmax", a, stream);
+}
+
+size_t silcu_sum_axis_workspace_bytes(size_t outer, size_t len, size_t inner) {
+  if (inner == 1) return 0;
+  const uint32_t sp = col_splits(outer, len, inner);
+  return sp > 1 ? size_t(sp) * outer * inner * sizeof(float) : 0;
+}
+
+silcu_status silcu_sum_axis_f32(const float *in, float *out, size_t outer, size_t len, size_t inner, void *ws,
+                                size_t wsb, silcu_stream stream) {
+  const size_t total = outer * inner;
+  if (total == 0) return SILCU_OK;
+  if (!in || !out) return fail(SILCU_INVALID_ARGUMENT, "sum_axis: null pointer");
+  cudaStream_t s = as_stream(stream);
+  if (len == 0) {
+    cudaError_t e = cudaMemsetAsync(out, 0, total * sizeof(float), s);
+    return e == cudaSuccess ? SILCU_OK : fail(SILCU_CUDA_ERROR, "sum_axis: %s", cudaGetErrorString(e));
+  }
+  if (inner == 1) {
+    if (len <= 256) {
+      const uint64_t blocks = (outer * 32 + 255) / 256;
+      sum_rows_warp_kernel<<<uint32_t(blocks), 256, 0, s>>>(in, out, outer, len);
+    } else {
+      const bool vec = (len % 4 == 0) && aligned16(in);
+      const uint64_t g = outer < 65535ull * 32 ? outer : 65535ull * 32;
+      sum_rows_kernel<<<uint32_t(g), 256, 0, s>>>(in, out, outer, len, vec);
+    }
+    return check_launch("sum_axis(rows)");
+  }
+  if (outer > 65535) return fail(SILCU_UNSUPPORTED, "sum_axis: outer extent > 65535");
+  const uint32_t sp = col_splits(outer, len, inner);
+  dim3 grid(uint32_t((inner + 255) / 256), uint32_t(outer), sp);
+  if (sp == 1) {
+    sum_cols_kernel<<<grid, 256, 0, s>>>(in, out, outer, len, inner, 1);
+  } else {
+    const size_t need = size_t(sp) * total * sizeof(float);
+    if (!ws || wsb < need) return fail(SILCU_WORKSPACE_TOO_SMALL, "sum_axis: workspace %zu < %zu", wsb, need);
+    float *part = static_cast<float *>(ws);
+    sum_cols_kernel<<<grid, 256, 0, s>>>(in, part, outer, len, inner, sp);
+    sum_cols_finish<<<uint32_t((total + 255) / 256), 256, 0, s>>>(part, out, total, sp);
+  }
+  return check_launch("sum_axis(cols)");
+}
+
+}  // extern "C"

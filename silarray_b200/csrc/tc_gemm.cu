@@ -1,0 +1,448 @@
+// fp32-faithful SGEMM on the 5th-generation tensor cores (sm_100a).
+//
+// Split precision (3xTF32, Ootomo & Yokota 2022, "Recovering single precision
+// accuracy from Tensor Cores while surpassing the FP32 theoretical peak
+// performance"): x = hi + lo with hi = tf32_rna(x), lo = x - hi (exact in
+// fp32), and  A.B ~= Ah.Bh + Ah.Bl + Al.Bh  accumulated in fp32 in TMEM.
+//
+// Pipeline, one 128x128 output tile per CTA:
+//   pack_split  (pre-pass) writes hi/lo copies of A and B, K-major, K padded
+//               to a multiple of 32, one pass over each operand;
+//   warp 0      TMA producer: 4 boxes of 128 rows x 32 fp32 (128 B, 128-byte
+//               swizzle) per K block into a 3-stage shared-memory ring;
+//   warp 1      allocates 128 TMEM columns, one thread issues
+//               tcgen05.mma.kind::tf32 (M=128, N=128, K=8) x 3 per K step and
+//               tcgen05.commit to release ring slots;
+//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns at a time, apply
+//               alpha / bias / activation / residual, store fp32 rows.
+// No TMA multicast and no clusters: each CTA loads its own tiles.
+// Every mbarrier wait is bounded (wall-clock limit via %globaltimer); on
+// expiry it records an error in the device error word and the CTA unwinds,
+// frees its TMEM and exits.
+#include <cuda.h>
+#include <string.h>
+
+#include "common.cuh"
+#include "gemm_internal.cuh"
+
+namespace silcu {
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
+constexpr int TILE_BYTES = BM * BK * 4;           // 16 KB, same for A and B boxes
+constexpr int STAGE_BYTES = 4 * TILE_BYTES;       // Ahi, Alo, Bhi, Blo
+constexpr int RING_BYTES = STAGES * STAGE_BYTES;  // 192 KB
+constexpr int SMEM_BYTES = RING_BYTES + 1024 + 256;
+constexpr int NUM_THREADS = 192;
+constexpr uint32_t TMEM_COLS = 128;
+constexpr int GROUP_M = 8;
+constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s per wait
+
+struct TcEpi {
+  float alpha;
+  const float *bias;
+  int64_t bias_len;
+  int act;
+  const float *residual;
+  int64_t ldr;
+};
+
+struct __align__(64) TcParams {
+  CUtensorMap a_hi, a_lo, b_hi, b_lo;  // 3-D {Kp, rows, batch}
+  float *C;
+  int64_t ldc, stride_c, bin, stride_c_in;
+  int M, N, Kp, tiles_m, tiles_n;
+  TcEpi epi;
+  int *err;
+};
+
+// ----------------------------------------------------------------- PTX glue
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait.  Returns false (and records `code`) when the phase does not
+// complete within WAIT_NS, or when another CTA already recorded an error.
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t i = 1;; i++) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0) {
+      if (*reinterpret_cast<volatile int *>(err) != 0) return false;
+      if (globaltimer() - t0 > WAIT_NS) {
+        atomicCAS(err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor, K-major operand with 128-byte swizzle:
+// 8-row x 128-byte swizzle atoms stacked along M/N every 1024 bytes (SBO);
+// LBO is unused for this layout (encoded as 1); version 1 (sm_100).
+__device__ __forceinline__ uint64_t make_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= uint64_t((addr & 0x3FFFFu) >> 4);
+  d |= uint64_t(1) << 16;
+  d |= uint64_t(1024 >> 4) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(2) << 61;
+  return d;
+}
+
+// Instruction descriptor: D fp32, A/B tf32, both K-major, N = BN, M = BM.
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) |
+                            (uint32_t(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accum));
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float epi_apply(const TcEpi &e, float acc, int64_t row, int64_t col,
+                                           const float *res) {
+  float v = acc;
+  if (e.alpha != 1.0f) v = __fmul_rn(v, e.alpha);
+  if (e.bias) v = __fadd_rn(v, __ldg(e.bias + (col % e.bias_len)));
+  if (e.act == SILCU_ACT_RELU) v = v >= 0.0f ? v : 0.0f;
+  else if (e.act == SILCU_ACT_SIGMOID) v = sigmoid_ref(v);
+  if (res) v = __fadd_rn(v, __ldg(res + row * e.ldr + col));
+  return v;
+}
+
+// ------------------------------------------------------------------- kernel
+__global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + RING_BYTES);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 1);
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES), accum_bar = smem_u32(bars + 2 * STAGES);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // Grouped raster inside one batch: GROUP_M tile-rows sweep the N tiles
+  // together so the A and B strips they share stay in L2.
+  const int tiles_per_batch = p.tiles_m * p.tiles_n;
+  const int bz = blockIdx.x / tiles_per_batch;
+  const int t = blockIdx.x % tiles_per_batch;
+  const int group = t / (GROUP_M * p.tiles_n);
+  const int first_m = group * GROUP_M;
+  const int gm = min(p.tiles_m - first_m, GROUP_M);
+  const int tm = first_m + (t % (GROUP_M * p.tiles_n)) % gm;
+  const int tn = (t % (GROUP_M * p.tiles_n)) / gm;
+  const int m0 = tm * BM, n0 = tn * BN;
+  const int nk = p.Kp / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    mbar_init(accum_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = 0; kb < nk; kb++) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        if (kb >= STAGES && !mbar_wait(empty0 + 8 * s, ph ^ 1, p.err, 1)) break;
+        const uint32_t full = full0 + 8 * s;
+        mbar_expect_tx(full, STAGE_BYTES);
+        const uint32_t dst = smem_u32(smem + s * STAGE_BYTES);
+        const int kc = kb * BK;
+        tma_load_3d(dst, &p.a_hi, full, kc, m0, bz);
+        tma_load_3d(dst + TILE_BYTES, &p.a_lo, full, kc, m0, bz);
+        tma_load_3d(dst + 2 * TILE_BYTES, &p.b_hi, full, kc, n0, bz);
+        tma_load_3d(dst + 3 * TILE_BYTES, &p.b_lo, full, kc, n0, bz);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = true;
+      for (int kb = 0; kb < nk && ok; kb++) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        if (!mbar_wait(full0 + 8 * s, ph, p.err, 2)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BK / 8; kk++) {
+          const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle atom
+          const uint64_t ah = make_desc(base + off), al = make_desc(base + TILE_BYTES + off);
+          const uint64_t bh = make_desc(base + 2 * TILE_BYTES + off), bl = make_desc(base + 3 * TILE_BYTES + off);
+          const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
+          mma_tf32(tmem, al, bh, first);  // small terms first
+          mma_tf32(tmem, ah, bl, 1u);
+          mma_tf32(tmem, ah, bh, 1u);
+        }
+        mma_commit(empty0 + 8 * s);
+      }
+      mma_commit(accum_bar);  // fires once every MMA issued above has completed
+    }
+  } else {
+    // Epilogue warps 2..5: TMEM lane quarter q = warp % 4 holds tile rows 32q..32q+31.
+    const int q = warp & 3;
+    bool ok = mbar_wait(accum_bar, 0, p.err, 3);
+    ok = ok && *reinterpret_cast<volatile int *>(p.err) == 0;
+    ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
+    tc_fence_after();
+    if (ok) {
+      const int64_t row = int64_t(m0) + 32 * q + lane;
+      const int64_t coff = (bz / p.bin) * p.stride_c + (bz % p.bin) * p.stride_c_in;
+      float *crow = p.C + coff + row * p.ldc;
+      const float *res = p.epi.residual ? p.epi.residual + coff : nullptr;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; c++) {
+        uint32_t r[32];
+        tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(32 * c), r);
+        if (row < p.M) {
+          const int64_t col0 = int64_t(n0) + 32 * c;
+          if (col0 + 32 <= p.N && (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(crow) & 15) == 0)) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              float4 o;
+              o.x = epi_apply(p.epi, __uint_as_float(r[j + 0]), row, col0 + j + 0, res);
+              o.y = epi_apply(p.epi, __uint_as_float(r[j + 1]), row, col0 + j + 1, res);
+              o.z = epi_apply(p.epi, __uint_as_float(r[j + 2]), row, col0 + j + 2, res);
+              o.w = epi_apply(p.epi, __uint_as_float(r[j + 3]), row, col0 + j + 3, res);
+              *reinterpret_cast<float4 *>(crow + col0 + j) = o;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+              if (col0 + j < p.N) crow[col0 + j] = epi_apply(p.epi, __uint_as_float(r[j]), row, col0 + j, res);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+  }
+}
+
+// ----------------------------------------------------------- split pre-pass
+// src element (b, r, k) at src + (b / bin)*sbatch + (b % bin)*sbatch_in + r*rs + k*ks
+// (one of rs/ks is 1).  Writes hi/lo[(b*rows + r)*Kp + k]; k in [K, Kp) is zero-filled.
+__global__ void __launch_bounds__(256) pack_split(const float *__restrict__ src, int64_t rs, int64_t ks,
+                                                  int64_t sbatch, int64_t bin, int64_t sbatch_in,
+                                                  int64_t rows, int64_t K, int64_t Kp,
+                                                  float *__restrict__ hi, float *__restrict__ lo) {
+  __shared__ float tile[32][33];
+  const int64_t b = blockIdx.z;
+  const int64_t r0 = int64_t(blockIdx.y) * 32, k0 = int64_t(blockIdx.x) * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+  const float *s = src + (b / bin) * sbatch + (b % bin) * sbatch_in;
+  if (ks == 1) {  // k contiguous: read along k
+    for (int i = ty; i < 32; i += 8) {
+      const int64_t r = r0 + i, k = k0 + tx;
+      tile[i][tx] = (r < rows && k < K) ? __ldg(s + r * rs + k) : 0.0f;
+    }
+  } else {  // r contiguous: read along r, transpose through shared memory
+    for (int i = ty; i < 32; i += 8) {
+      const int64_t k = k0 + i, r = r0 + tx;
+      tile[tx][i] = (r < rows && k < K) ? __ldg(s + r * rs + k * ks) : 0.0f;
+    }
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int64_t r = r0 + i, k = k0 + tx;
+    if (r < rows && k < Kp) {
+      const float x = tile[i][tx];
+      uint32_t h;
+      asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+      const float xh = __uint_as_float(h);
+      const size_t o = size_t(b * rows + r) * size_t(Kp) + size_t(k);
+      hi[o] = xh;
+      lo[o] = __fsub_rn(x, xh);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+bool make_map(CUtensorMap *m, const float *base, int64_t Kp, int64_t rows, int64_t batch) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {cuuint64_t(Kp), cuuint64_t(rows), cuuint64_t(batch)};
+  cuuint64_t strides[2] = {cuuint64_t(Kp) * 4, cuuint64_t(Kp) * 4 * cuuint64_t(rows)};
+  cuuint32_t box[3] = {BK, BM, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int64_t padded_k(int64_t K) { return ((K + BK - 1) / BK) * BK; }
+
+}  // namespace
+
+int64_t total_batch(const silcu_gemm_args &a) { return a.batch * (a.batch_inner > 1 ? a.batch_inner : 1); }
+
+size_t tc_workspace_bytes(const silcu_gemm_args &a) {
+  const int64_t Kp = padded_k(a.K > 0 ? a.K : 1);
+  return size_t(2) * size_t(Kp) * size_t(total_batch(a)) * size_t(a.M + a.N) * sizeof(float) + 256;
+}
+
+silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t s) {
+  const int64_t Kp = padded_k(a.K > 0 ? a.K : 1);
+  const size_t need = tc_workspace_bytes(a);
+  if (!ws || wsb < need) return fail(SILCU_WORKSPACE_TOO_SMALL, "sgemm(tc): workspace %zu < %zu", wsb, need);
+  if (a.M > (1 << 30) || a.N > (1 << 30) || Kp > (1 << 30))
+    return fail(SILCU_UNSUPPORTED, "sgemm(tc): extent >= 2^30");
+  const int64_t tiles_m = (a.M + BM - 1) / BM, tiles_n = (a.N + BN - 1) / BN;
+  const int64_t nb = total_batch(a), bin = a.batch_inner > 1 ? a.batch_inner : 1;
+  if (tiles_m * tiles_n * nb > 0x7FFFFFFF) return fail(SILCU_UNSUPPORTED, "sgemm(tc): too many tiles");
+  if (nb > 65535) return fail(SILCU_UNSUPPORTED, "sgemm(tc): batch > 65535");
+  float *base = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(ws) + 255) & ~uintptr_t(255));
+  const size_t a_elems = size_t(nb) * a.M * Kp, b_elems = size_t(nb) * a.N * Kp;
+  float *a_hi = base, *a_lo = a_hi + a_elems, *b_hi = a_lo + a_elems, *b_lo = b_hi + b_elems;
+
+  // A: rows m, k.  Non-transposed: (m, k) at m*lda + k.  Transposed: k*lda + m.
+  {
+    const int64_t rs = a.trans_a ? 1 : a.lda, ks = a.trans_a ? a.lda : 1;
+    dim3 g(uint32_t(Kp / 32), uint32_t((a.M + 31) / 32), uint32_t(nb));
+    pack_split<<<g, 256, 0, s>>>(a.A, rs, ks, a.stride_a, bin, a.stride_a_inner, a.M, a.K, Kp, a_hi, a_lo);
+  }
+  // B as rows n, k.  Non-transposed B [K,N]: (n, k) at k*ldb + n.  Transposed [N,K]: n*ldb + k.
+  {
+    const int64_t rs = a.trans_b ? a.ldb : 1, ks = a.trans_b ? 1 : a.ldb;
+    dim3 g(uint32_t(Kp / 32), uint32_t((a.N + 31) / 32), uint32_t(nb));
+    pack_split<<<g, 256, 0, s>>>(a.B, rs, ks, a.stride_b, bin, a.stride_b_inner, a.N, a.K, Kp, b_hi, b_lo);
+  }
+  silcu_status st = check_launch("sgemm(tc) pack");
+  if (st != SILCU_OK) return st;
+
+  TcParams p;
+  memset(&p, 0, sizeof(p));
+  if (!make_map(&p.a_hi, a_hi, Kp, a.M, nb) || !make_map(&p.a_lo, a_lo, Kp, a.M, nb) ||
+      !make_map(&p.b_hi, b_hi, Kp, a.N, nb) || !make_map(&p.b_lo, b_lo, Kp, a.N, nb))
+    return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed");
+  p.C = a.C;
+  p.ldc = a.ldc;
+  p.stride_c = a.stride_c;
+  p.bin = bin;
+  p.stride_c_in = a.stride_c_inner;
+  p.M = int(a.M);
+  p.N = int(a.N);
+  p.Kp = int(Kp);
+  p.tiles_m = int(tiles_m);
+  p.tiles_n = int(tiles_n);
+  p.epi.alpha = a.alpha;
+  p.epi.bias = a.bias;
+  p.epi.bias_len = a.bias_len > 0 ? a.bias_len : 1;
+  p.epi.act = a.act;
+  p.epi.residual = a.residual;
+  p.epi.ldr = a.ldr;
+  p.err = device_error_ptr();
+  if (!p.err) return fail(SILCU_CUDA_ERROR, "sgemm(tc): no device error word");
+
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return fail(SILCU_CUDA_ERROR, "sgemm(tc): smem attribute: %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  const uint32_t grid = uint32_t(tiles_m * tiles_n * nb);
+  tc_gemm_kernel<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(p);
+  return check_launch("sgemm(tc)");
+}
+
+}  // namespace silcu

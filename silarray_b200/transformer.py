@@ -1,0 +1,181 @@
+"""Pre-norm transformer block forward on the B200 backend.
+
+The block is the graph of the reference's bench/composite/bench_transformer.cpp:56-67
+(layer_norm -> Q/K/V linear -> Q.K^T * scale -> softmax -> .V -> linear(Wo)
+-> residual -> layer_norm -> linear(W1).relu() -> linear(W2) -> residual),
+generalised to a batch of sequences and multi-head attention (scale
+1/sqrt(head_dim), attention per (sequence, head)).
+
+Each reference node maps onto one launch of include/silcu.h, with the
+reference's elementwise nodes folded into GEMM epilogues where they follow a
+dot (bias add, the `* scale` affine node, relu, the residual add); the
+rounding sequence per element is the reference's (dot, then + bias, then
+act, then + residual).  Q, K and V come from one GEMM against [Wq|Wk|Wv]
+(columns are independent, so the values equal three separate GEMMs).
+
+Launches per forward: layer_norm, QKV gemm, scores gemm (batched over
+sequence x head with strided views), softmax, context gemm, Wo gemm
+(+bias +residual), layer_norm, W1 gemm (+bias, relu), W2 gemm (+bias
++residual).  Every GEMM is the 3xTF32 tcgen05 kernel plus its split pre-pass.
+"""
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import gpu
+
+
+@dataclass
+class Config:
+    batch: int = 32
+    seq: int = 512
+    d_model: int = 768
+    heads: int = 12
+    d_ff: int = 3072
+    eps: float = 1e-5
+
+    @property
+    def head_dim(self):
+        return self.d_model // self.heads
+
+    @property
+    def tokens(self):
+        return self.batch * self.seq
+
+    def gemm_flops(self):
+        """Algorithmic FLOPs of one forward (2*M*N*K summed over the GEMMs)."""
+        T, d, f, S, h = self.tokens, self.d_model, self.d_ff, self.seq, self.head_dim
+        qkv = 2 * T * d * 3 * d
+        attn = 2 * (2 * self.batch * self.heads * S * S * h)
+        wo = 2 * T * d * d
+        ffn = 2 * (2 * T * d * f)
+        return qkv + attn + wo + ffn
+
+
+PARAM_NAMES = ("g1", "be1", "wq", "bq", "wk", "bk", "wv", "bv", "wo", "bo",
+               "g2", "be2", "w1", "b1", "w2", "b2")
+
+
+def _normal(rng, shape, std):
+    return (rng.standard_normal(shape, dtype=np.float32) * np.float32(std)).astype(np.float32)
+
+
+def init_params(cfg, seed=0):
+    """Weights ~ N(0, 0.02^2), biases 0, gamma 1, beta 0 (the benchmark config)."""
+    rng = np.random.default_rng(seed)
+    d, f = cfg.d_model, cfg.d_ff
+    p = {
+        "g1": np.ones(d, np.float32), "be1": np.zeros(d, np.float32),
+        "g2": np.ones(d, np.float32), "be2": np.zeros(d, np.float32),
+        "bq": np.zeros(d, np.float32), "bk": np.zeros(d, np.float32), "bv": np.zeros(d, np.float32),
+        "bo": np.zeros(d, np.float32), "b1": np.zeros(f, np.float32), "b2": np.zeros(d, np.float32),
+    }
+    for k in ("wq", "wk", "wv", "wo"):
+        p[k] = _normal(rng, (d, d), 0.02)
+    p["w1"] = _normal(rng, (d, f), 0.02)
+    p["w2"] = _normal(rng, (f, d), 0.02)
+    return p
+
+
+def init_input(cfg, seed=1):
+    """Activations ~ N(0, 1), [batch*seq, d_model]."""
+    rng = np.random.default_rng(seed)
+    return rng.standard_normal((cfg.tokens, cfg.d_model), dtype=np.float32)
+
+
+class Block:
+    """Device-resident weights plus preallocated activations for one config."""
+
+    def __init__(self, cfg, params, device="cuda"):
+        self.cfg = cfg
+        self.dev = torch.device(device)
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(self.dev)  # noqa: E731
+        d = cfg.d_model
+        self.g1, self.be1, self.g2, self.be2 = t(params["g1"]), t(params["be1"]), t(params["g2"]), t(params["be2"])
+        self.wqkv = t(np.concatenate([params["wq"], params["wk"], params["wv"]], axis=1))  # [d, 3d]
+        self.bqkv = t(np.concatenate([params["bq"], params["bk"], params["bv"]]))
+        self.wo, self.bo = t(params["wo"]), t(params["bo"])
+        self.w1, self.b1 = t(params["w1"]), t(params["b1"])
+        self.w2, self.b2 = t(params["w2"]), t(params["b2"])
+        T, f, S, H = cfg.tokens, cfg.d_ff, cfg.seq, cfg.heads
+        e = lambda *s: torch.empty(*s, dtype=torch.float32, device=self.dev)  # noqa: E731
+        self.h = e(T * d)
+        self.qkv = e(T * 3 * d)
+        self.scores = e(cfg.batch * H * S * S)
+        self.ctx = e(T * d)
+        self.r1 = e(T * d)
+        self.ff = e(T * f)
+        self.scale = float(np.float32(1.0) / np.sqrt(np.float32(cfg.head_dim)))
+
+    def forward(self, x, out=None):
+        cfg = self.cfg
+        T, d, f, S, H, hd, B = cfg.tokens, cfg.d_model, cfg.d_ff, cfg.seq, cfg.heads, cfg.head_dim, cfg.batch
+        x = x.reshape(-1)
+        out = torch.empty(T * d, dtype=torch.float32, device=self.dev) if out is None else out
+        gpu.layer_norm(x, self.h, self.g1, self.be1, T, d, cfg.eps)
+        gpu.gemm(self.h, self.wqkv, self.qkv, M=T, N=3 * d, K=d, bias=self.bqkv)
+        # scores[b, h] = Q_bh . K_bh^T * scale   (Q_bh rows: qkv[b*S + s, h*hd : h*hd+hd])
+        gpu.gemm(self.qkv, self.qkv[d:], self.scores, M=S, N=S, K=hd, lda=3 * d, ldb=3 * d,
+                 trans_b=True, batch=B, stride_a=S * 3 * d, stride_b=S * 3 * d, stride_c=H * S * S,
+                 batch_inner=H, stride_a_inner=hd, stride_b_inner=hd, stride_c_inner=S * S,
+                 alpha=self.scale)
+        gpu.softmax(self.scores, self.scores, B * H * S, S)
+        # ctx[b*S + s, h*hd + j] = (attn_bh . V_bh)[s, j]
+        gpu.gemm(self.scores, self.qkv[2 * d:], self.ctx, M=S, N=hd, K=S, lda=S, ldb=3 * d, ldc=d,
+                 batch=B, stride_a=H * S * S, stride_b=S * 3 * d, stride_c=S * d,
+                 batch_inner=H, stride_a_inner=S * S, stride_b_inner=hd, stride_c_inner=hd)
+        gpu.gemm(self.ctx, self.wo, self.r1, M=T, N=d, K=d, bias=self.bo, residual=x)
+        gpu.layer_norm(self.r1, self.h, self.g2, self.be2, T, d, cfg.eps)
+        gpu.gemm(self.h, self.w1, self.ff, M=T, N=f, K=d, bias=self.b1, act="relu")
+        gpu.gemm(self.ff, self.w2, out, M=T, N=d, K=f, bias=self.b2, residual=self.r1)
+        return out.reshape(T, d)
+
+
+def reference_forward(cfg, params, x):
+    """CPU reference of the same block: the reference's own CPU build when it
+    is present (oracle/_ref, every op a sil:: array op), else the oracle
+    restatement composed the same way.  Test infrastructure only."""
+    import oracle as O
+    if O.ref is not None:
+        return O.ref.transformer_block(x, cfg.batch, cfg.seq, cfg.d_model, cfg.heads, cfg.d_ff, params)
+    return _restated_forward(cfg, params, x)
+
+
+def _restated_forward(cfg, p, x):
+    import oracle as O
+    S, d, H, hd = cfg.seq, cfg.d_model, cfg.heads, cfg.head_dim
+    scale = np.float32(1.0) / np.sqrt(np.float32(hd))
+    out = np.empty_like(x)
+    lin = lambda a, w, b: O.binary("add", O.sgemm(a, w), b).reshape(a.shape[0], w.shape[1])  # noqa: E731
+    for bi in range(cfg.batch):
+        X = x[bi * S:(bi + 1) * S]
+        h = O.layer_norm(X, p["g1"], p["be1"])
+        Q, K, V = lin(h, p["wq"], p["bq"]), lin(h, p["wk"], p["bk"]), lin(h, p["wv"], p["bv"])
+        ctx = np.empty((S, d), np.float32)
+        for hh in range(H):
+            sl = slice(hh * hd, (hh + 1) * hd)
+            q, k, v = (np.ascontiguousarray(m[:, sl]) for m in (Q, K, V))
+            sc = O.scalar_op("mul", scale, O.sgemm(q, k, tb=True)).reshape(S, S)
+            at = O.softmax(sc)
+            ctx[:, sl] = O.sgemm(at, v)
+        r1 = O.binary("add", X, lin(ctx, p["wo"], p["bo"])).reshape(S, d)
+        h2 = O.layer_norm(r1, p["g2"], p["be2"])
+        ff = O.relu(lin(h2, p["w1"], p["b1"]))
+        out[bi * S:(bi + 1) * S] = O.binary("add", r1, lin(ff, p["w2"], p["b2"])).reshape(S, d)
+    return out
+
+
+def check_parity(got, ref, cfg):
+    """End-to-end tolerance for the 6-GEMM chain: |g - r| <= 2e-4 * (1 + |r|)
+    (each GEMM is within sqrt(K) * (1e-6 + 1e-5|r|) of the oracle; layer_norm
+    and softmax amplify the differences by O(1) factors)."""
+    got = np.asarray(got, np.float64).reshape(ref.shape)
+    ref = np.asarray(ref, np.float64)
+    err = np.abs(got - ref)
+    lim = 2e-4 * (1.0 + np.abs(ref))
+    if not (err <= lim).all():
+        i = int(np.argmax(err - lim))
+        raise AssertionError(f"transformer parity: {(err > lim).sum()} of {err.size} outside; worst "
+                             f"got {got.ravel()[i]!r} ref {ref.ravel()[i]!r}; max err {err.max():.3e}")
+    return float(err.max())

@@ -1,0 +1,117 @@
+"""GEMM family on the GPU vs the oracle (fp64-accumulated reference GEMM):
+|g - r| <= sqrt(K) * (1e-6 + 1e-5 |r|) for both the CUDA-core FFMA path and
+the tcgen05 3xTF32 path; epilogues (bias / relu / sigmoid / alpha /
+residual) with the reference's per-node rounding."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from silarray_b200 import gpu
+from tests._tol import assert_close, assert_dot_close
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+SHAPES = [(128, 128, 32), (256, 384, 96), (200, 130, 70), (1, 4096, 4096), (32, 768, 4096),
+          (7, 300, 129), (513, 257, 1000), (64, 64, 64), (1000, 33, 5)]
+
+
+@pytest.mark.parametrize("algo", ["ffma", "tc", "auto"])
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_gemm_nn(cuda, algo, M, N, K):
+    rng = np.random.default_rng(M * 7 + N * 3 + K)
+    a = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    b = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    got = host(gpu.gemm(dev(a), dev(b), M=M, N=N, K=K, algo=algo)).reshape(M, N)
+    assert_dot_close(got, O.sgemm(a, b), K, what=f"{algo} {M}x{N}x{K}")
+
+
+@pytest.mark.parametrize("algo", ["ffma", "tc"])
+@pytest.mark.parametrize("ta,tb", [(False, True), (True, False), (True, True)])
+def test_gemm_transposed(cuda, algo, ta, tb):
+    M, N, K = 190, 260, 150
+    rng = np.random.default_rng(5)
+    a = rng.uniform(-1, 1, (K, M) if ta else (M, K)).astype(np.float32)
+    b = rng.uniform(-1, 1, (N, K) if tb else (K, N)).astype(np.float32)
+    got = host(gpu.gemm(dev(a), dev(b), M=M, N=N, K=K, trans_a=ta, trans_b=tb, algo=algo)).reshape(M, N)
+    assert_dot_close(got, O.sgemm(a, b, ta=ta, tb=tb), K, what=f"{algo} t{int(ta)}{int(tb)}")
+
+
+@pytest.mark.parametrize("algo", ["ffma", "tc"])
+def test_gemm_batched(cuda, algo):
+    S = np.load(__import__("os").path.join(__import__("os").path.dirname(__file__), "golden", "seeded.npz"))
+    a, b = S["bmm_a"], S["bmm_b"]
+    B, M, K = a.shape
+    N = b.shape[2]
+    got = host(gpu.gemm(dev(a), dev(b), M=M, N=N, K=K, batch=B, stride_a=M * K, stride_b=K * N,
+                        stride_c=M * N, algo=algo)).reshape(B, M, N)
+    assert_dot_close(got, S["batched_dot"], K, what="batched golden")
+    # attention-shaped: NT per (batch*head), 16 x [300 x 64] . [64 x 300]^T
+    rng = np.random.default_rng(8)
+    q = rng.normal(0, 1, (16, 300, 64)).astype(np.float32)
+    k = rng.normal(0, 1, (16, 300, 64)).astype(np.float32)
+    got = host(gpu.gemm(dev(q), dev(k), M=300, N=300, K=64, trans_b=True, batch=16, stride_a=300 * 64,
+                        stride_b=300 * 64, stride_c=300 * 300, alpha=0.125, algo=algo)).reshape(16, 300, 300)
+    for i in (0, 7, 15):
+        ref = O.scalar_op("mul", 0.125, O.sgemm(q[i], k[i], tb=True)).reshape(300, 300)
+        assert_dot_close(got[i], ref, 64, what="nt batch")
+
+
+@pytest.mark.parametrize("algo", ["ffma", "tc", "auto"])
+def test_gemm_epilogues(cuda, algo):
+    S = np.load(__import__("os").path.join(__import__("os").path.dirname(__file__), "golden", "seeded.npz"))
+    a, b, bias = S["dot_a"], S["dot_b"], S["lin_b"]
+    M, K = a.shape
+    N = b.shape[1]
+    lin = host(gpu.gemm(dev(a), dev(b), M=M, N=N, K=K, bias=dev(bias), algo=algo)).reshape(M, N)
+    assert_dot_close(lin, S["linear"], K, what="linear")
+    sg = host(gpu.gemm(dev(a), dev(b), M=M, N=N, K=K, bias=dev(bias), act="sigmoid", algo=algo)).reshape(M, N)
+    assert_dot_close(sg, S["linear_sigmoid"], K, what="linear_sigmoid")
+    rl = host(gpu.gemm(dev(a), dev(b), M=M, N=N, K=K, bias=dev(bias), act="relu", algo=algo)).reshape(M, N)
+    assert_dot_close(rl, O.relu(S["linear"]), K, what="linear relu")
+    res = np.random.default_rng(3).normal(0, 1, (M, N)).astype(np.float32)
+    rr = host(gpu.gemm(dev(a), dev(b), M=M, N=N, K=K, bias=dev(bias), residual=dev(res), algo=algo)).reshape(M, N)
+    assert_dot_close(rr, O.binary("add", S["linear"], res).reshape(M, N), K, what="linear + residual")
+
+
+def test_reference_argument_forms(cuda):
+    """gpu::sgemm / sgemm_bias / sgemm_bias_sigmoid / sgemv argument lists."""
+    x = np.array([[1, 2, 3], [4, 5, 6]], np.float32)
+    W = np.array([[1, 2], [3, 4], [5, 6]], np.float32)
+    b = np.array([10, 20], np.float32)
+    C = torch.empty(4, device="cuda")
+    gpu.sgemm_bias(dev(x), dev(W), C, dev(b), 2, 2, 2, 3, 3, 2)
+    np.testing.assert_array_equal(host(C), [32, 48, 59, 84])  # test/test_array.cpp:262-268
+    gpu.sgemm(dev(x), dev(W), C, 2, 2, 3, 3, 2)
+    np.testing.assert_array_equal(host(C), [22, 28, 49, 64])
+    rng = np.random.default_rng(0)
+    xv = rng.normal(0, 1, 4096).astype(np.float32)
+    Wv = rng.normal(0, 0.02, (4096, 4096)).astype(np.float32)
+    bv = rng.normal(0, 0.01, 4096).astype(np.float32)
+    y = torch.empty(4096, device="cuda")
+    gpu.sgemv(dev(xv), dev(Wv), y, 4096, 4096, bias=dev(bv))
+    ref = O.binary("add", O.sgemm(xv.reshape(1, -1), Wv).ravel(), bv)
+    assert_dot_close(host(y), ref, 4096, what="gemv")
+
+
+def test_tc_large_sampled_rows(cuda):
+    """2048^3 on the tensor-core path, checked on sampled rows against fp64."""
+    n = 2048
+    rng = np.random.default_rng(0)
+    a = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+    b = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+    got = host(gpu.gemm(dev(a), dev(b), M=n, N=n, K=n, algo="tc")).reshape(n, n)
+    rows = [0, 1, 127, 128, 1000, 2047]
+    ref = a[rows].astype(np.float64) @ b.astype(np.float64)
+    assert_dot_close(got[rows], ref, n, what="tc 2048 sampled")
+    gpu.device_status()
