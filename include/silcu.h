@@ -38,6 +38,8 @@ typedef struct CUstream_st *silcu_stream; /* == cudaStream_t */
 const char *silcu_last_error(void);
 /* ABI version, bumped on any signature change. */
 int silcu_abi_version(void);
+/* Number of kernels this library has launched in this process (all devices). */
+unsigned long long silcu_kernel_launches(void);
 /* Blocks until `stream` is idle; replaces synchronize() (include/gpu.h:1375-1377)
  * and gpu_context::flush() (include/gpu.h:107-123). */
 silcu_status silcu_synchronize(silcu_stream stream);

@@ -55,6 +55,7 @@ class GemmArgs(C.Structure):
 _SIGS = {
     "silcu_last_error": ([], C.c_char_p),
     "silcu_abi_version": ([], C.c_int),
+    "silcu_kernel_launches": ([], C.c_ulonglong),
     "silcu_synchronize": ([vp], C.c_int),
     "silcu_device_status": ([vp], C.c_int),
     "silcu_sigmoid_f32": ([vp, vp, sz, vp], C.c_int),

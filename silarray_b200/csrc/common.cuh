@@ -18,8 +18,8 @@ silcu_status fail(silcu_status st, const char *fmt, ...);
 // Device address of the error word that bounded waits set (per device).
 int *device_error_ptr();
 
-// Maps the launch's cudaGetLastError() into a status.
-silcu_status check_launch(const char *what);
+// Counts `launches` kernel launches and maps cudaGetLastError() into a status.
+silcu_status check_launch(const char *what, int launches = 1);
 
 inline cudaStream_t as_stream(silcu_stream s) {
   return reinterpret_cast<cudaStream_t>(s);

@@ -24,6 +24,32 @@ __device__ __forceinline__ float bin(float x, float y) {
   return powf(x, y);
 }
 
+// (int)std::pow(double(x), double(y)) as the reference's int path computes it
+// (include/cpu.h:215-237), evaluated exactly: the power is an integer, so
+// repeated multiplication in double is exact while it stays below 2^53, and
+// any result outside int32 converts like x86-64's cvttsd2si (INT32_MIN).
+__device__ __forceinline__ int32_t ipow_ref(int32_t x, int32_t y) {
+  if (y < 0) {
+    if (x == 1) return 1;
+    if (x == -1) return (y & 1) ? -1 : 1;
+    if (x == 0) return INT32_MIN;  // 1/0 = inf
+    return 0;                      // |1/x^k| < 1 truncates to 0
+  }
+  double r = 1.0, b = double(x);
+  uint32_t e = uint32_t(y);
+  while (e) {
+    if (e & 1u) r *= b;
+    e >>= 1;
+    if (e) b *= b;
+    if (fabs(r) > 2147483648.0 || fabs(b) > 9.0e15) {
+      // the exact result leaves int32 unless the remaining factors are +-1/0
+      if (fabs(double(x)) > 1.0) return INT32_MIN;
+    }
+  }
+  if (r >= 2147483648.0 || r < -2147483648.0) return INT32_MIN;
+  return int32_t(r);
+}
+
 template <int OP>
 __device__ __forceinline__ int32_t bin(int32_t x, int32_t y) {
   uint32_t ux = static_cast<uint32_t>(x), uy = static_cast<uint32_t>(y);
@@ -31,7 +57,7 @@ __device__ __forceinline__ int32_t bin(int32_t x, int32_t y) {
   if (OP == kSub) return static_cast<int32_t>(ux - uy);
   if (OP == kMul) return static_cast<int32_t>(ux * uy);
   if (OP == kDiv) return y == 0 ? 0 : (y == -1 ? static_cast<int32_t>(0u - ux) : x / y);
-  return static_cast<int32_t>(pow(static_cast<double>(x), static_cast<double>(y)));
+  return ipow_ref(x, y);
 }
 
 // Loads 4 values of a broadcast operand starting at logical index i.

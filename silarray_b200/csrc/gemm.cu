@@ -291,7 +291,7 @@ void launch_skinny(const SkinnyPlan &pl, const float *X, int64_t ldx, const floa
 }
 
 bool skinny_eligible(const silcu_gemm_args &a) {
-  return a.M <= 16 && !a.trans_a && !a.trans_b && a.batch == 1 && a.batch_inner <= 1 && (a.ldb % 4 == 0) &&
+  return a.M <= 64 && !a.trans_a && !a.trans_b && a.batch == 1 && a.batch_inner <= 1 && (a.ldb % 4 == 0) &&
          aligned16(a.B) && a.K >= 1;
 }
 
@@ -374,7 +374,7 @@ silcu_status silcu_sgemm_ex(const silcu_gemm_args *ap, void *ws, size_t wsb, sil
       case 8: launch_skinny<8>(pl, a.A, a.lda, a.B, a.ldb, a.C, a.ldc, a.M, a.N, a.K, part, epi, s); break;
       default: launch_skinny<16>(pl, a.A, a.lda, a.B, a.ldb, a.C, a.ldc, a.M, a.N, a.K, part, epi, s); break;
     }
-    return check_launch("sgemm(skinny)");
+    return check_launch("sgemm(skinny)", pl.splits > 1 ? 2 : 1);
   }
   const int64_t bin = a.batch_inner > 1 ? a.batch_inner : 1;
   if (a.batch * bin > 65535) return fail(SILCU_UNSUPPORTED, "sgemm(ffma): batch > 65535");

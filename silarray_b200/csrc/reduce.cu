@@ -33,6 +33,17 @@ __device__ __forceinline__ T block_reduce(T v, T *smem, F op) {
   return r;
 }
 
+// Row reduction: a whole warp per row (WARP) or the whole CTA.
+template <int NT, bool WARP, typename T, typename F>
+__device__ __forceinline__ T row_reduce(T v, T *smem, F op) {
+  if (WARP) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+  }
+  return block_reduce<NT>(v, smem, op);
+}
+
 struct Add {
   template <typename T>
   __device__ T operator()(T a, T b) const { return a + b; }
@@ -199,7 +210,7 @@ silcu_status run_reduce(const char *name, const In *in, size_t n, Out *out, floa
   cudaStream_t s = as_stream(stream);
   reduce_partials<KIND, In><<<g, kRedThreads, 0, s>>>(in, n, part);
   reduce_finish<KIND, Out><<<1, 1024, 0, s>>>(part, g, out, out_value, reinterpret_cast<const float *>(in));
-  return check_launch(name);
+  return check_launch(name, 2);
 }
 
 // ------------------------------------------------------------------ row ops
@@ -214,15 +225,19 @@ struct RowArgs {
   float eps;
 };
 
-// One CTA per row, the row cached in registers: VPT float4 per thread.
-// Requires cols % 4 == 0 and 16-byte aligned rows; cols <= NT * VPT * 4.
-template <int OP, int NT, int VPT>
-__global__ void __launch_bounds__(NT) row_kernel(const RowArgs a) {
+// The row cached in registers: VPT float4 per thread.  WARP: one warp per
+// row, 8 rows per CTA of 256 threads (short rows, shuffle-only reductions);
+// otherwise one CTA of NT threads per row.
+// Requires cols % 4 == 0 and 16-byte aligned rows; cols <= (WARP ? 32 : NT) * VPT * 4.
+template <int OP, int NT, int VPT, bool WARP>
+__global__ void __launch_bounds__(WARP ? 256 : NT) row_kernel(const RowArgs a) {
   __shared__ float sf[NT / 32];
   __shared__ unsigned long long sk[NT / 32];
   const uint32_t c4 = a.cols / 4;
-  const int t = threadIdx.x;
-  for (uint32_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+  const int t = WARP ? (threadIdx.x & 31) : threadIdx.x;
+  const uint32_t rows_per_cta = WARP ? 8u : 1u;
+  const uint32_t row0 = WARP ? blockIdx.x * 8u + (threadIdx.x >> 5) : blockIdx.x;
+  for (uint32_t row = row0; row < a.rows; row += gridDim.x * rows_per_cta) {
     const float4 *src = reinterpret_cast<const float4 *>(a.in + size_t(row) * a.cols);
     float4 v[VPT];
 #pragma unroll
@@ -235,7 +250,7 @@ __global__ void __launch_bounds__(NT) row_kernel(const RowArgs a) {
 #pragma unroll
       for (int j = 0; j < VPT; j++)
         if (t + j * NT < c4) m = fmaxf(m, fmaxf(fmaxf(v[j].x, v[j].y), fmaxf(v[j].z, v[j].w)));
-      m = block_reduce<NT>(m, sf, Max());
+      m = row_reduce<NT, WARP>(m, sf, Max());
       float s = 0.f;
 #pragma unroll
       for (int j = 0; j < VPT; j++) {
@@ -247,7 +262,7 @@ __global__ void __launch_bounds__(NT) row_kernel(const RowArgs a) {
           s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
         }
       }
-      s = block_reduce<NT>(s, sf, Add());
+      s = row_reduce<NT, WARP>(s, sf, Add());
       const float inv = __frcp_rn(s);
       float4 *dst = reinterpret_cast<float4 *>(a.out + size_t(row) * a.cols);
 #pragma unroll
@@ -261,7 +276,7 @@ __global__ void __launch_bounds__(NT) row_kernel(const RowArgs a) {
       float s = 0.f;
 #pragma unroll
       for (int j = 0; j < VPT; j++) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
-      s = block_reduce<NT>(s, sf, Add());
+      s = row_reduce<NT, WARP>(s, sf, Add());
       const float mu = __fdiv_rn(s, float(a.cols));
       float ss = 0.f;
 #pragma unroll
@@ -275,7 +290,7 @@ __global__ void __launch_bounds__(NT) row_kernel(const RowArgs a) {
                 (__fmul_rn(v[j].z, v[j].z) + __fmul_rn(v[j].w, v[j].w));
         }
       }
-      ss = block_reduce<NT>(ss, sf, Add());
+      ss = row_reduce<NT, WARP>(ss, sf, Add());
       const float inv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(a.cols)), a.eps)));
       float4 *dst = reinterpret_cast<float4 *>(a.out + size_t(row) * a.cols);
       const float4 *g4 = reinterpret_cast<const float4 *>(a.gamma);
@@ -308,7 +323,7 @@ __global__ void __launch_bounds__(NT) row_kernel(const RowArgs a) {
           best = best > k0 ? best : k0;
         }
       }
-      best = block_reduce<NT>(best, sk, Max());
+      best = row_reduce<NT, WARP>(best, sk, Max());
       if (t == 0) a.idx[row] = best ? int32_t(0xFFFFFFFFu - uint32_t(best & 0xFFFFFFFFu)) : 0;
     }
   }
@@ -363,7 +378,13 @@ __global__ void __launch_bounds__(512) row_kernel_generic(const RowArgs a) {
 template <int OP, int NT, int VPT>
 void launch_row(const RowArgs &a, cudaStream_t s) {
   uint32_t g = a.rows;
-  row_kernel<OP, NT, VPT><<<g, NT, 0, s>>>(a);
+  row_kernel<OP, NT, VPT, false><<<g, NT, 0, s>>>(a);
+}
+
+template <int OP, int VPT>
+void launch_row_warp(const RowArgs &a, cudaStream_t s) {
+  uint32_t g = (a.rows + 7) / 8;
+  row_kernel<OP, 32, VPT, true><<<g, 256, 0, s>>>(a);
 }
 
 template <int OP>
@@ -373,9 +394,10 @@ silcu_status run_rows(const char *name, const RowArgs &a, silcu_stream stream) {
   const bool vec = (a.cols % 4 == 0) && aligned16(a.in) && (!a.out || aligned16(a.out)) &&
                    (OP != kLayerNorm || (aligned16(a.gamma) && aligned16(a.beta)));
   const uint32_t c = a.cols;
-  if (vec && c <= 128) launch_row<OP, 32, 1>(a, s);
-  else if (vec && c <= 512) launch_row<OP, 64, 2>(a, s);
-  else if (vec && c <= 1024) launch_row<OP, 128, 2>(a, s);
+  if (vec && c <= 128) launch_row_warp<OP, 1>(a, s);
+  else if (vec && c <= 256) launch_row_warp<OP, 2>(a, s);
+  else if (vec && c <= 512) launch_row_warp<OP, 4>(a, s);
+  else if (vec && c <= 1024) launch_row_warp<OP, 8>(a, s);
   else if (vec && c <= 2048) launch_row<OP, 256, 2>(a, s);
   else if (vec && c <= 4096) launch_row<OP, 256, 4>(a, s);
   else if (vec && c <= 8192) launch_row<OP, 512, 4>(a, s);
@@ -572,7 +594,7 @@ silcu_status silcu_argmax_f32(const float *in, int32_t *out, size_t rows, size_t
                                                                    static_cast<unsigned long long *>(ws));
     argmax_split_finish<<<uint32_t((rows + 255) / 256), 256, 0, s>>>(
         static_cast<const unsigned long long *>(ws), uint32_t(rows), sp, out);
-    return check_launch("argmax(split)");
+    return check_launch("argmax(split)", 2);
   }
   RowArgs a{in, nullptr, out, nullptr, nullptr, uint32_t(rows), uint32_t(cols), 0.f};
   return run_rows<kRowArgmax>("argmax", a, stream);
@@ -616,6 +638,7 @@ silcu_status silcu_sum_axis_f32(const float *in, float *out, size_t outer, size_
     float *part = static_cast<float *>(ws);
     sum_cols_kernel<<<grid, 256, 0, s>>>(in, part, outer, len, inner, sp);
     sum_cols_finish<<<uint32_t((total + 255) / 256), 256, 0, s>>>(part, out, total, sp);
+    return check_launch("sum_axis(cols)", 2);
   }
   return check_launch("sum_axis(cols)");
 }

@@ -45,7 +45,10 @@ int *device_error_ptr() {
   return cached[dev];
 }
 
-silcu_status check_launch(const char *what) {
+static unsigned long long g_launches = 0;
+
+silcu_status check_launch(const char *what, int launches) {
+  __atomic_fetch_add(&g_launches, (unsigned long long)launches, __ATOMIC_RELAXED);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(SILCU_CUDA_ERROR, "%s: %s", what, cudaGetErrorString(e));
   return SILCU_OK;
@@ -58,6 +61,10 @@ extern "C" {
 const char *silcu_last_error(void) { return silcu::g_last_error; }
 
 int silcu_abi_version(void) { return 1; }
+
+unsigned long long silcu_kernel_launches(void) {
+  return __atomic_load_n(&silcu::g_launches, __ATOMIC_RELAXED);
+}
 
 silcu_status silcu_synchronize(silcu_stream stream) {
   cudaError_t e = cudaStreamSynchronize(silcu::as_stream(stream));

@@ -34,7 +34,8 @@ constexpr int STAGE_BYTES = 4 * TILE_BYTES;       // Ahi, Alo, Bhi, Blo
 constexpr int RING_BYTES = STAGES * STAGE_BYTES;  // 192 KB
 constexpr int SMEM_BYTES = RING_BYTES + 1024 + 256;
 constexpr int NUM_THREADS = 192;
-constexpr uint32_t TMEM_COLS = 128;
+constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulator buffers
+constexpr int CHUNK_KB = 1;              // K blocks per TMEM accumulation chunk
 constexpr int GROUP_M = 8;
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s per wait
 
@@ -176,12 +177,22 @@ __device__ __forceinline__ float epi_apply(const TcEpi &e, float acc, int64_t ro
 }
 
 // ------------------------------------------------------------------- kernel
+// Accumulation is split in two levels (the remedy of Ootomo & Yokota for the
+// tensor core's truncating fp32 accumulation): the MMAs of CHUNK_KB K blocks
+// accumulate into one of two TMEM buffers; the epilogue warps drain each
+// finished chunk into fp32 registers with round-to-nearest adds while the
+// MMAs continue in the other buffer.
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + RING_BYTES);
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 1);
-  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES), accum_bar = smem_u32(bars + 2 * STAGES);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
+  const uint32_t tfull0 = smem_u32(bars + 2 * STAGES), tempty0 = smem_u32(bars + 2 * STAGES + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -197,13 +208,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
   const int tn = (t % (GROUP_M * p.tiles_n)) / gm;
   const int m0 = tm * BM, n0 = tn * BN;
   const int nk = p.Kp / BK;
+  const int nchunks = (nk + CHUNK_KB - 1) / CHUNK_KB;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
     }
-    mbar_init(accum_bar, 1);
+    for (int j = 0; j < 2; j++) {
+      mbar_init(tfull0 + 8 * j, 1);
+      mbar_init(tempty0 + 8 * j, 4);  // one arrive per epilogue warp
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -235,59 +250,82 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
   } else if (warp == 1) {
     if (lane == 0) {
       bool ok = true;
-      for (int kb = 0; kb < nk && ok; kb++) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (!mbar_wait(full0 + 8 * s, ph, p.err, 2)) { ok = false; break; }
+      for (int c = 0; c < nchunks && ok; c++) {
+        const int j = c & 1;
+        const uint32_t use = c >> 1;
+        if (c >= 2 && !mbar_wait(tempty0 + 8 * j, (use & 1) ^ 1, p.err, 4)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+        const uint32_t dacc = tmem + uint32_t(j * BN);
+        const int kb1 = min(nk, (c + 1) * CHUNK_KB);
+        for (int kb = c * CHUNK_KB; kb < kb1; kb++) {
+          const int s = kb % STAGES;
+          const uint32_t ph = (kb / STAGES) & 1;
+          if (!mbar_wait(full0 + 8 * s, ph, p.err, 2)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < BK / 8; kk++) {
-          const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle atom
-          const uint64_t ah = make_desc(base + off), al = make_desc(base + TILE_BYTES + off);
-          const uint64_t bh = make_desc(base + 2 * TILE_BYTES + off), bl = make_desc(base + 3 * TILE_BYTES + off);
-          const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
-          mma_tf32(tmem, al, bh, first);  // small terms first
-          mma_tf32(tmem, ah, bl, 1u);
-          mma_tf32(tmem, ah, bh, 1u);
+          for (int kk = 0; kk < BK / 8; kk++) {
+            const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle atom
+            const uint64_t ah = make_desc(base + off), al = make_desc(base + TILE_BYTES + off);
+            const uint64_t bh = make_desc(base + 2 * TILE_BYTES + off), bl = make_desc(base + 3 * TILE_BYTES + off);
+            const uint32_t first = (kb == c * CHUNK_KB && kk == 0) ? 0u : 1u;
+            mma_tf32(dacc, al, bh, first);  // small terms first
+            mma_tf32(dacc, ah, bl, 1u);
+            mma_tf32(dacc, ah, bh, 1u);
+          }
+          mma_commit(empty0 + 8 * s);
         }
-        mma_commit(empty0 + 8 * s);
+        mma_commit(tfull0 + 8 * j);  // fires when this chunk's MMAs have completed
       }
-      mma_commit(accum_bar);  // fires once every MMA issued above has completed
     }
   } else {
     // Epilogue warps 2..5: TMEM lane quarter q = warp % 4 holds tile rows 32q..32q+31.
     const int q = warp & 3;
-    bool ok = mbar_wait(accum_bar, 0, p.err, 3);
+    float acc[BN];
+#pragma unroll
+    for (int i = 0; i < BN; i++) acc[i] = 0.0f;
+    bool ok = true;
+    for (int c = 0; c < nchunks; c++) {
+      const int j = c & 1;
+      const uint32_t use = c >> 1;
+      bool w = mbar_wait(tfull0 + 8 * j, use & 1, p.err, 3);
+      w = __all_sync(0xffffffffu, w);  // tcgen05.ld below is warp-collective
+      if (!w) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t src = tmem + (uint32_t(32 * q) << 16) + uint32_t(j * BN);
+#pragma unroll
+      for (int cc = 0; cc < BN / 32; cc++) {
+        uint32_t r[32];
+        tmem_ld32(src + uint32_t(32 * cc), r);
+#pragma unroll
+        for (int i = 0; i < 32; i++) acc[32 * cc + i] = __fadd_rn(acc[32 * cc + i], __uint_as_float(r[i]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty0 + 8 * j);
+    }
     ok = ok && *reinterpret_cast<volatile int *>(p.err) == 0;
-    ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
-    tc_fence_after();
-    if (ok) {
-      const int64_t row = int64_t(m0) + 32 * q + lane;
+    ok = __all_sync(0xffffffffu, ok);
+    const int64_t row = int64_t(m0) + 32 * q + lane;
+    if (ok && row < p.M) {
       const int64_t coff = (bz / p.bin) * p.stride_c + (bz % p.bin) * p.stride_c_in;
       float *crow = p.C + coff + row * p.ldc;
       const float *res = p.epi.residual ? p.epi.residual + coff : nullptr;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; c++) {
-        uint32_t r[32];
-        tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(32 * c), r);
-        if (row < p.M) {
-          const int64_t col0 = int64_t(n0) + 32 * c;
-          if (col0 + 32 <= p.N && (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(crow) & 15) == 0)) {
+      const bool vec = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(crow) & 15) == 0);
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              float4 o;
-              o.x = epi_apply(p.epi, __uint_as_float(r[j + 0]), row, col0 + j + 0, res);
-              o.y = epi_apply(p.epi, __uint_as_float(r[j + 1]), row, col0 + j + 1, res);
-              o.z = epi_apply(p.epi, __uint_as_float(r[j + 2]), row, col0 + j + 2, res);
-              o.w = epi_apply(p.epi, __uint_as_float(r[j + 3]), row, col0 + j + 3, res);
-              *reinterpret_cast<float4 *>(crow + col0 + j) = o;
-            }
-          } else {
+      for (int c = 0; c < BN / 4; c++) {
+        const int64_t col0 = int64_t(n0) + 4 * c;
+        if (vec && col0 + 4 <= p.N) {
+          float4 o;
+          o.x = epi_apply(p.epi, acc[4 * c + 0], row, col0 + 0, res);
+          o.y = epi_apply(p.epi, acc[4 * c + 1], row, col0 + 1, res);
+          o.z = epi_apply(p.epi, acc[4 * c + 2], row, col0 + 2, res);
+          o.w = epi_apply(p.epi, acc[4 * c + 3], row, col0 + 3, res);
+          *reinterpret_cast<float4 *>(crow + col0) = o;
+        } else {
 #pragma unroll
-            for (int j = 0; j < 32; j++)
-              if (col0 + j < p.N) crow[col0 + j] = epi_apply(p.epi, __uint_as_float(r[j]), row, col0 + j, res);
-          }
+          for (int e = 0; e < 4; e++)
+            if (col0 + e < p.N) crow[col0 + e] = epi_apply(p.epi, acc[4 * c + e], row, col0 + e, res);
         }
       }
     }
@@ -405,7 +443,7 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
     dim3 g(uint32_t(Kp / 32), uint32_t((a.N + 31) / 32), uint32_t(nb));
     pack_split<<<g, 256, 0, s>>>(a.B, rs, ks, a.stride_b, bin, a.stride_b_inner, a.N, a.K, Kp, b_hi, b_lo);
   }
-  silcu_status st = check_launch("sgemm(tc) pack");
+  silcu_status st = check_launch("sgemm(tc) pack", 2);
   if (st != SILCU_OK) return st;
 
   TcParams p;
