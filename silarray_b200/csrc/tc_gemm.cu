@@ -5,21 +5,25 @@
 // performance"): x = hi + lo with hi = tf32_rna(x), lo = x - hi (exact in
 // fp32), and  A.B ~= Ah.Bh + Ah.Bl + Al.Bh  accumulated in fp32 in TMEM.
 //
-// Pipeline, one 128x128 output tile per CTA:
+// Pipeline (persistent: one CTA per SM walks 128x128 output tiles):
 //   pack_split  (pre-pass) writes hi/lo copies of A and B, K-major, K padded
 //               to a multiple of 32, one pass over each operand;
 //   warp 0      TMA producer: 4 boxes of 128 rows x 32 fp32 (128 B, 128-byte
 //               swizzle) per K block into a 3-stage shared-memory ring;
-//   warp 1      allocates 128 TMEM columns, one thread issues
-//               tcgen05.mma.kind::tf32 (M=128, N=128, K=8) x 3 per K step and
-//               tcgen05.commit to release ring slots;
-//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns at a time, apply
-//               alpha / bias / activation / residual, store fp32 rows.
+//   warp 1      allocates all 512 TMEM columns (4 accumulator buffers of 128),
+//               one thread issues tcgen05.mma.kind::tf32 (M=128, N=128, K=8)
+//               x 3 per K step and tcgen05.commit to release ring slots and to
+//               hand each finished chunk of CHUNK_KB K blocks to the epilogue;
+//   warps 2-5   drain each chunk with tcgen05.ld into fp32 registers (round to
+//               nearest), and at the end of a tile stage 32x32 blocks through
+//               shared memory so that the alpha / bias / activation / residual
+//               epilogue and the stores are coalesced 128-byte row segments.
 // No TMA multicast and no clusters: each CTA loads its own tiles.
 // Every mbarrier wait is bounded (wall-clock limit via %globaltimer); on
 // expiry it records an error in the device error word and the CTA unwinds,
 // frees its TMEM and exits.
 #include <cuda.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "common.cuh"
@@ -32,10 +36,13 @@ constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
 constexpr int TILE_BYTES = BM * BK * 4;           // 16 KB, same for A and B boxes
 constexpr int STAGE_BYTES = 4 * TILE_BYTES;       // Ahi, Alo, Bhi, Blo
 constexpr int RING_BYTES = STAGES * STAGE_BYTES;  // 192 KB
-constexpr int SMEM_BYTES = RING_BYTES + 1024 + 256;
+constexpr int STAGE_PITCH = 33;                            // floats per staged row (bank-conflict free)
+constexpr int OUT_STAGE_BYTES = 4 * 32 * STAGE_PITCH * 4;  // one 32x32 block per epilogue warp
+constexpr int SMEM_BYTES = RING_BYTES + OUT_STAGE_BYTES + 1024 + 256;
 constexpr int NUM_THREADS = 192;
-constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulator buffers
-constexpr int CHUNK_KB = 1;              // K blocks per TMEM accumulation chunk
+constexpr int NBUF = 4;                        // TMEM accumulator buffers (chunks in flight)
+constexpr uint32_t TMEM_COLS = NBUF * BN;      // 512 columns: all of TMEM, one CTA per SM
+constexpr int CHUNK_KB_DEFAULT = 4;      // K blocks per TMEM accumulation chunk
 constexpr int GROUP_M = 8;
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s per wait
 
@@ -52,7 +59,7 @@ struct __align__(64) TcParams {
   CUtensorMap a_hi, a_lo, b_hi, b_lo;  // 3-D {Kp, rows, batch}
   float *C;
   int64_t ldc, stride_c, bin, stride_c_in;
-  int M, N, Kp, tiles_m, tiles_n;
+  int M, N, Kp, tiles_m, tiles_n, nbatch, chunk_kb;
   TcEpi epi;
   int *err;
 };
@@ -151,7 +158,7 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
                : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
@@ -162,8 +169,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
         "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ float epi_apply(const TcEpi &e, float acc, int64_t row, int64_t col,
                                            const float *res) {
@@ -186,28 +194,43 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-__global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + RING_BYTES);
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
-  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
-  const uint32_t tfull0 = smem_u32(bars + 2 * STAGES), tempty0 = smem_u32(bars + 2 * STAGES + 2);
+struct Tile {
+  int bz, m0, n0;
+};
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  // Grouped raster inside one batch: GROUP_M tile-rows sweep the N tiles
-  // together so the A and B strips they share stay in L2.
+// Grouped raster inside one batch: GROUP_M tile-rows sweep the N tiles
+// together so the A and B strips they share stay in L2.
+__device__ __forceinline__ Tile decode_tile(const TcParams &p, int idx) {
   const int tiles_per_batch = p.tiles_m * p.tiles_n;
-  const int bz = blockIdx.x / tiles_per_batch;
-  const int t = blockIdx.x % tiles_per_batch;
+  Tile r;
+  r.bz = idx / tiles_per_batch;
+  const int t = idx % tiles_per_batch;
   const int group = t / (GROUP_M * p.tiles_n);
   const int first_m = group * GROUP_M;
   const int gm = min(p.tiles_m - first_m, GROUP_M);
   const int tm = first_m + (t % (GROUP_M * p.tiles_n)) % gm;
   const int tn = (t % (GROUP_M * p.tiles_n)) / gm;
-  const int m0 = tm * BM, n0 = tn * BN;
+  r.m0 = tm * BM;
+  r.n0 = tn * BN;
+  return r;
+}
+
+// Persistent: CTA i takes tiles i, i + gridDim.x, ...  The TMA ring, the MMA
+// chunk buffers and the epilogue run as one continuous stream across tiles,
+// so a tile's pipeline fill and its output store overlap its neighbours'.
+__global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float *ostage = reinterpret_cast<float *>(smem + RING_BYTES);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + RING_BYTES + OUT_STAGE_BYTES);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 2 * NBUF);
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
+  const uint32_t tfull0 = smem_u32(bars + 2 * STAGES), tempty0 = smem_u32(bars + 2 * STAGES + NBUF);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total_tiles = p.tiles_m * p.tiles_n * p.nbatch;
   const int nk = p.Kp / BK;
+  const int CHUNK_KB = p.chunk_kb;
   const int nchunks = (nk + CHUNK_KB - 1) / CHUNK_KB;
 
   if (threadIdx.x == 0) {
@@ -215,7 +238,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
     }
-    for (int j = 0; j < 2; j++) {
+    for (int j = 0; j < NBUF; j++) {
       mbar_init(tfull0 + 8 * j, 1);
       mbar_init(tempty0 + 8 * j, 4);  // one arrive per epilogue warp
     }
@@ -233,100 +256,116 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int kb = 0; kb < nk; kb++) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (kb >= STAGES && !mbar_wait(empty0 + 8 * s, ph ^ 1, p.err, 1)) break;
-        const uint32_t full = full0 + 8 * s;
-        mbar_expect_tx(full, STAGE_BYTES);
-        const uint32_t dst = smem_u32(smem + s * STAGE_BYTES);
-        const int kc = kb * BK;
-        tma_load_3d(dst, &p.a_hi, full, kc, m0, bz);
-        tma_load_3d(dst + TILE_BYTES, &p.a_lo, full, kc, m0, bz);
-        tma_load_3d(dst + 2 * TILE_BYTES, &p.b_hi, full, kc, n0, bz);
-        tma_load_3d(dst + 3 * TILE_BYTES, &p.b_lo, full, kc, n0, bz);
+      uint32_t kbg = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        const Tile tl = decode_tile(p, tile);
+        for (int kb = 0; kb < nk; kb++, kbg++) {
+          const uint32_t s = kbg % STAGES;
+          const uint32_t ph = (kbg / STAGES) & 1;
+          if (kbg >= STAGES && !mbar_wait(empty0 + 8 * s, ph ^ 1, p.err, 1)) { ok = false; break; }
+          const uint32_t full = full0 + 8 * s;
+          mbar_expect_tx(full, STAGE_BYTES);
+          const uint32_t dst = smem_u32(smem + s * STAGE_BYTES);
+          const int kc = kb * BK;
+          tma_load_3d(dst, &p.a_hi, full, kc, tl.m0, tl.bz);
+          tma_load_3d(dst + TILE_BYTES, &p.a_lo, full, kc, tl.m0, tl.bz);
+          tma_load_3d(dst + 2 * TILE_BYTES, &p.b_hi, full, kc, tl.n0, tl.bz);
+          tma_load_3d(dst + 3 * TILE_BYTES, &p.b_lo, full, kc, tl.n0, tl.bz);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
+      uint32_t kbg = 0, cg = 0;
       bool ok = true;
-      for (int c = 0; c < nchunks && ok; c++) {
-        const int j = c & 1;
-        const uint32_t use = c >> 1;
-        if (c >= 2 && !mbar_wait(tempty0 + 8 * j, (use & 1) ^ 1, p.err, 4)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t dacc = tmem + uint32_t(j * BN);
-        const int kb1 = min(nk, (c + 1) * CHUNK_KB);
-        for (int kb = c * CHUNK_KB; kb < kb1; kb++) {
-          const int s = kb % STAGES;
-          const uint32_t ph = (kb / STAGES) & 1;
-          if (!mbar_wait(full0 + 8 * s, ph, p.err, 2)) { ok = false; break; }
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        for (int c = 0; c < nchunks && ok; c++, cg++) {
+          const uint32_t j = cg % NBUF, use = cg / NBUF;
+          if (cg >= NBUF && !mbar_wait(tempty0 + 8 * j, (use & 1) ^ 1, p.err, 4)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t dacc = tmem + j * BN;
+          const int kb1 = min(nk, (c + 1) * CHUNK_KB);
+          for (int kb = c * CHUNK_KB; kb < kb1; kb++, kbg++) {
+            const uint32_t s = kbg % STAGES;
+            const uint32_t ph = (kbg / STAGES) & 1;
+            if (!mbar_wait(full0 + 8 * s, ph, p.err, 2)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < BK / 8; kk++) {
-            const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle atom
-            const uint64_t ah = make_desc(base + off), al = make_desc(base + TILE_BYTES + off);
-            const uint64_t bh = make_desc(base + 2 * TILE_BYTES + off), bl = make_desc(base + 3 * TILE_BYTES + off);
-            const uint32_t first = (kb == c * CHUNK_KB && kk == 0) ? 0u : 1u;
-            mma_tf32(dacc, al, bh, first);  // small terms first
-            mma_tf32(dacc, ah, bl, 1u);
-            mma_tf32(dacc, ah, bh, 1u);
+            for (int kk = 0; kk < BK / 8; kk++) {
+              const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle atom
+              const uint64_t ah = make_desc(base + off), al = make_desc(base + TILE_BYTES + off);
+              const uint64_t bh = make_desc(base + 2 * TILE_BYTES + off), bl = make_desc(base + 3 * TILE_BYTES + off);
+              const uint32_t first = (kb == c * CHUNK_KB && kk == 0) ? 0u : 1u;
+              mma_tf32(dacc, al, bh, first);  // small terms first
+              mma_tf32(dacc, ah, bl, 1u);
+              mma_tf32(dacc, ah, bh, 1u);
+            }
+            mma_commit(empty0 + 8 * s);
           }
-          mma_commit(empty0 + 8 * s);
+          mma_commit(tfull0 + 8 * j);  // fires when this chunk's MMAs have completed
         }
-        mma_commit(tfull0 + 8 * j);  // fires when this chunk's MMAs have completed
       }
     }
   } else {
     // Epilogue warps 2..5: TMEM lane quarter q = warp % 4 holds tile rows 32q..32q+31.
     const int q = warp & 3;
-    float acc[BN];
-#pragma unroll
-    for (int i = 0; i < BN; i++) acc[i] = 0.0f;
+    uint32_t cg = 0;
     bool ok = true;
-    for (int c = 0; c < nchunks; c++) {
-      const int j = c & 1;
-      const uint32_t use = c >> 1;
-      bool w = mbar_wait(tfull0 + 8 * j, use & 1, p.err, 3);
-      w = __all_sync(0xffffffffu, w);  // tcgen05.ld below is warp-collective
-      if (!w) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t src = tmem + (uint32_t(32 * q) << 16) + uint32_t(j * BN);
+    for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+      const Tile tl = decode_tile(p, tile);
+      float acc[BN];
 #pragma unroll
-      for (int cc = 0; cc < BN / 32; cc++) {
-        uint32_t r[32];
-        tmem_ld32(src + uint32_t(32 * cc), r);
+      for (int i = 0; i < BN; i++) acc[i] = 0.0f;
+      for (int c = 0; c < nchunks; c++, cg++) {
+        const uint32_t j = cg % NBUF, use = cg / NBUF;
+        bool w = mbar_wait(tfull0 + 8 * j, use & 1, p.err, 3);
+        w = __all_sync(0xffffffffu, w);  // tcgen05.ld below is warp-collective
+        if (!w) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t src = tmem + (uint32_t(32 * q) << 16) + j * BN;
 #pragma unroll
-        for (int i = 0; i < 32; i++) acc[32 * cc + i] = __fadd_rn(acc[32 * cc + i], __uint_as_float(r[i]));
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(tempty0 + 8 * j);
-    }
-    ok = ok && *reinterpret_cast<volatile int *>(p.err) == 0;
-    ok = __all_sync(0xffffffffu, ok);
-    const int64_t row = int64_t(m0) + 32 * q + lane;
-    if (ok && row < p.M) {
-      const int64_t coff = (bz / p.bin) * p.stride_c + (bz % p.bin) * p.stride_c_in;
-      float *crow = p.C + coff + row * p.ldc;
-      const float *res = p.epi.residual ? p.epi.residual + coff : nullptr;
-      const bool vec = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(crow) & 15) == 0);
+        for (int cc = 0; cc < BN / 32; cc += 2) {
+          uint32_t r0[32], r1[32];
+          tmem_ld32_nowait(src + uint32_t(32 * cc), r0);
+          tmem_ld32_nowait(src + uint32_t(32 * cc + 32), r1);
+          tmem_ld_wait();
 #pragma unroll
-      for (int c = 0; c < BN / 4; c++) {
-        const int64_t col0 = int64_t(n0) + 4 * c;
-        if (vec && col0 + 4 <= p.N) {
-          float4 o;
-          o.x = epi_apply(p.epi, acc[4 * c + 0], row, col0 + 0, res);
-          o.y = epi_apply(p.epi, acc[4 * c + 1], row, col0 + 1, res);
-          o.z = epi_apply(p.epi, acc[4 * c + 2], row, col0 + 2, res);
-          o.w = epi_apply(p.epi, acc[4 * c + 3], row, col0 + 3, res);
-          *reinterpret_cast<float4 *>(crow + col0) = o;
-        } else {
-#pragma unroll
-          for (int e = 0; e < 4; e++)
-            if (col0 + e < p.N) crow[col0 + e] = epi_apply(p.epi, acc[4 * c + e], row, col0 + e, res);
+          for (int i = 0; i < 32; i++) {
+            acc[32 * cc + i] = __fadd_rn(acc[32 * cc + i], __uint_as_float(r0[i]));
+            acc[32 * cc + 32 + i] = __fadd_rn(acc[32 * cc + 32 + i], __uint_as_float(r1[i]));
+          }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty0 + 8 * j);
+      }
+      const bool good = __all_sync(0xffffffffu, ok && *reinterpret_cast<volatile int *>(p.err) == 0);
+      if (!good) break;
+      // Store: each warp owns rows 32q..32q+31 of the tile.  Per 32-column
+      // block, lanes write their row into a padded shared-memory block, then
+      // read it back by column so that every global access (store, bias,
+      // residual) is one coalesced 128-byte row segment.
+      float *st = ostage + q * 32 * STAGE_PITCH;
+      const int64_t coff = (tl.bz / p.bin) * p.stride_c + (tl.bz % p.bin) * p.stride_c_in;
+      float *cbase = p.C + coff;
+      const float *res = p.epi.residual ? p.epi.residual + coff : nullptr;
+      const int64_t col = int64_t(tl.n0) + lane;
+#pragma unroll
+      for (int cb = 0; cb < BN / 32; cb++) {
+#pragma unroll
+        for (int i = 0; i < 32; i++) st[lane * STAGE_PITCH + i] = acc[32 * cb + i];
+        __syncwarp();
+        const int64_t c = col + 32 * cb;
+        if (c < p.N) {
+#pragma unroll 4
+          for (int r = 0; r < 32; r++) {
+            const int64_t row = int64_t(tl.m0) + 32 * q + r;
+            if (row < p.M) cbase[row * p.ldc + c] = epi_apply(p.epi, st[r * STAGE_PITCH + lane], row, c, res);
+          }
+        }
+        __syncwarp();
       }
     }
   }
@@ -461,6 +500,12 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
   p.Kp = int(Kp);
   p.tiles_m = int(tiles_m);
   p.tiles_n = int(tiles_n);
+  p.nbatch = int(nb);
+  p.chunk_kb = CHUNK_KB_DEFAULT;
+  if (const char *env = getenv("SILCU_TC_CHUNK_KB")) {  // tuning knob: K blocks per accumulation chunk
+    const int v = atoi(env);
+    if (v >= 1) p.chunk_kb = v;
+  }
   p.epi.alpha = a.alpha;
   p.epi.bias = a.bias;
   p.epi.bias_len = a.bias_len > 0 ? a.bias_len : 1;
@@ -478,7 +523,8 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
     if (e != cudaSuccess) return fail(SILCU_CUDA_ERROR, "sgemm(tc): smem attribute: %s", cudaGetErrorString(e));
     configured[dev] = true;
   }
-  const uint32_t grid = uint32_t(tiles_m * tiles_n * nb);
+  const int64_t total = tiles_m * tiles_n * nb;
+  const uint32_t grid = uint32_t(total < sm_count() ? total : sm_count());
   tc_gemm_kernel<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(p);
   return check_launch("sgemm(tc)");
 }
