@@ -124,6 +124,16 @@ silcu_status silcu_fused_f32(const silcu_program *prog_host, const float *const 
  * quirk of include/array.h:1733-1740 (values <= FLT_MIN never win; 0 if none). */
 size_t silcu_reduce_workspace_bytes(size_t n);
 silcu_status silcu_sum_f32(const float *in, size_t n, float *out, void *workspace, size_t workspace_bytes, silcu_stream stream);
+/* Same result as silcu_sum_f32, but takes no workspace and allocates nothing.
+ * No counterpart in the reference: it is for callers that cannot allocate
+ * device memory (code running inside an allocator or memory-pool callback, or
+ * a plugin whose host forbids cudaMalloc after start-up).  Scratch is a fixed
+ * 32 KiB array inside the library (4096 fp64 partials) on every GPU that
+ * loads it; inputs needing more partials are rejected with SILCU_UNSUPPORTED.
+ * The first call on a device looks up that array's address (make it before
+ * any stream capture).  All calls share the array: calls that overlap on the
+ * GPU (different streams, no ordering between them) race. */
+silcu_status silcu_sum_f32_noalloc(const float *in, size_t n, float *out, silcu_stream stream);
 silcu_status silcu_min_f32(const float *in, size_t n, float *out, void *workspace, size_t workspace_bytes, silcu_stream stream);
 silcu_status silcu_max_f32(const float *in, size_t n, float *out, void *workspace, size_t workspace_bytes, silcu_stream stream);
 silcu_status silcu_sum_i32(const int32_t *in, size_t n, int32_t *out, void *workspace, size_t workspace_bytes, silcu_stream stream);

@@ -66,6 +66,7 @@ _SIGS = {
     "silcu_fused_f32": ([C.POINTER(Program), C.POINTER(vp), C.POINTER(sz), vp, sz, vp], C.c_int),
     "silcu_reduce_workspace_bytes": ([sz], sz),
     "silcu_sum_f32": ([vp, sz, vp, vp, sz, vp], C.c_int),
+    "silcu_sum_f32_noalloc": ([vp, sz, vp, vp], C.c_int),
     "silcu_min_f32": ([vp, sz, vp, vp, sz, vp], C.c_int),
     "silcu_max_f32": ([vp, sz, vp, vp, sz, vp], C.c_int),
     "silcu_sum_i32": ([vp, sz, vp, vp, sz, vp], C.c_int),

@@ -644,3 +644,61 @@ silcu_status silcu_sum_axis_f32(const float *in, float *out, size_t outer, size_
 }
 
 }  // extern "C"
+
+// ------------------------------------------------ allocation-free whole sum
+// For callers that may not allocate device memory themselves: code running
+// inside a host application's custom allocator or memory-pool callback, or a
+// plugin whose host forbids cudaMalloc after start-up.  The scratch for the
+// first pass lives in a fixed array compiled into this library instead of a
+// caller-provided workspace.
+namespace silcu {
+namespace {
+
+// One fp64 partial per CTA of the first pass: 4096 x 8 B = 32 KiB, held on
+// every GPU that loads this library until the process exits.
+constexpr int kNoAllocPartials = 4096;
+static __device__ __align__(256) double g_noalloc_partials[kNoAllocPartials];
+
+// Host code must not pass the symbol itself to a kernel (on the host it is a
+// stand-in, not a device address); look the address up once per device.
+double *noalloc_partials(silcu_status *st) {
+  static double *cached[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    *st = fail(SILCU_CUDA_ERROR, "sum_f32_noalloc: no current device");
+    return nullptr;
+  }
+  if (!cached[dev]) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+    if (e != cudaSuccess) {
+      *st = fail(SILCU_CUDA_ERROR, "sum_f32_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    cached[dev] = static_cast<double *>(p);
+  }
+  *st = SILCU_OK;
+  return cached[dev];
+}
+
+}  // namespace
+}  // namespace silcu
+
+extern "C" silcu_status silcu_sum_f32_noalloc(const float *in, size_t n, float *out, silcu_stream stream) {
+  if (!in || !out) return fail(SILCU_INVALID_ARGUMENT, "sum_f32_noalloc: null pointer");
+  if (n == 0) return fail(SILCU_INVALID_ARGUMENT, "sum_f32_noalloc: empty input");
+  const int g = red_grid(n);
+  if (g > kNoAllocPartials)
+    return fail(SILCU_UNSUPPORTED, "sum_f32_noalloc: needs %d partials, the built-in scratch holds %d", g,
+                kNoAllocPartials);
+  silcu_status st;
+  double *part = noalloc_partials(&st);
+  if (!part) return st;
+  // Every CTA of the first pass overwrites its own partial before the finish
+  // kernel reads it, so nothing left over from an earlier call is read.
+  cudaStream_t s = as_stream(stream);
+  reduce_partials<kSum, float><<<g, kRedThreads, 0, s>>>(in, n, part);
+  reduce_finish<kSum, float><<<1, 1024, 0, s>>>(part, g, out, nullptr, in);
+  return check_launch("sum_f32_noalloc", 2);
+}
