@@ -32,16 +32,32 @@
 namespace silcu {
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
-constexpr int TILE_BYTES = BM * BK * 4;           // 16 KB, same for A and B boxes
-constexpr int STAGE_BYTES = 4 * TILE_BYTES;       // Ahi, Alo, Bhi, Blo
-constexpr int RING_BYTES = STAGES * STAGE_BYTES;  // 192 KB
-constexpr int STAGE_PITCH = 33;                            // floats per staged row (bank-conflict free)
-constexpr int OUT_STAGE_BYTES = 4 * 32 * STAGE_PITCH * 4;  // one 32x32 block per epilogue warp
-constexpr int SMEM_BYTES = RING_BYTES + OUT_STAGE_BYTES + 1024 + 256;
-constexpr int NUM_THREADS = 192;
-constexpr int NBUF = 4;                        // TMEM accumulator buffers (chunks in flight)
-constexpr uint32_t TMEM_COLS = NBUF * BN;      // 512 columns: all of TMEM, one CTA per SM
+constexpr int BM = 128, BK = 32;
+constexpr int STAGE_PITCH = 33;  // floats per staged output row (bank-conflict free)
+
+// Per-variant constants: BN = 128 (3-stage ring, 4 TMEM chunk buffers, 4
+// epilogue warps) or BN = 256 (2-stage ring, 2 chunk buffers, 8 epilogue
+// warps, each owning 128 columns).  The wider tile halves the shared-memory
+// operand traffic per FLOP of A, which bounds the 128-wide variant.
+template <int BN_>
+struct Cfg {
+  static constexpr int BN = BN_;
+  static constexpr int TILE_A = BM * BK * 4;
+  static constexpr int TILE_B = BN * BK * 4;
+  static constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_B;  // Ahi, Alo, Bhi, Blo
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
+  static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int EPI_WARPS = BN / 32;
+  static constexpr int OUT_STAGE_BYTES = EPI_WARPS * 32 * STAGE_PITCH * 4;
+  static constexpr int SMEM_BYTES = RING_BYTES + OUT_STAGE_BYTES + 1024 + 256;
+  static constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int NBUF = 512 / BN;  // TMEM accumulator buffers (chunks in flight)
+  static constexpr uint32_t TMEM_COLS = 512;
+  // Instruction descriptor: D fp32, A/B tf32, both K-major, N = BN, M = BM.
+  static constexpr uint32_t IDESC =
+      (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+};
 constexpr int CHUNK_KB_DEFAULT = 4;      // K blocks per TMEM accumulation chunk
 constexpr int GROUP_M = 8;
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s per wait
@@ -141,16 +157,13 @@ __device__ __forceinline__ uint64_t make_desc(uint32_t addr) {
   return d;
 }
 
-// Instruction descriptor: D fp32, A/B tf32, both K-major, N = BN, M = BM.
-constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) |
-                            (uint32_t(BM >> 4) << 24);
-
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accum) {
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accum) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accum));
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum));
 }
 
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
@@ -200,6 +213,7 @@ struct Tile {
 
 // Grouped raster inside one batch: GROUP_M tile-rows sweep the N tiles
 // together so the A and B strips they share stay in L2.
+template <int BN>
 __device__ __forceinline__ Tile decode_tile(const TcParams &p, int idx) {
   const int tiles_per_batch = p.tiles_m * p.tiles_n;
   Tile r;
@@ -218,11 +232,16 @@ __device__ __forceinline__ Tile decode_tile(const TcParams &p, int idx) {
 // Persistent: CTA i takes tiles i, i + gridDim.x, ...  The TMA ring, the MMA
 // chunk buffers and the epilogue run as one continuous stream across tiles,
 // so a tile's pipeline fill and its output store overlap its neighbours'.
-__global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
+template <int BN_>
+__global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
+  using C = Cfg<BN_>;
+  constexpr int BN = C::BN, STAGES = C::STAGES, NBUF = C::NBUF, RING_BYTES = C::RING_BYTES;
+  constexpr int STAGE_BYTES = C::STAGE_BYTES, TILE_A = C::TILE_A, TILE_B = C::TILE_B;
+  constexpr uint32_t TMEM_COLS = C::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float *ostage = reinterpret_cast<float *>(smem + RING_BYTES);
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + RING_BYTES + OUT_STAGE_BYTES);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + RING_BYTES + C::OUT_STAGE_BYTES);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 2 * NBUF);
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
   const uint32_t tfull0 = smem_u32(bars + 2 * STAGES), tempty0 = smem_u32(bars + 2 * STAGES + NBUF);
@@ -240,7 +259,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
     }
     for (int j = 0; j < NBUF; j++) {
       mbar_init(tfull0 + 8 * j, 1);
-      mbar_init(tempty0 + 8 * j, 4);  // one arrive per epilogue warp
+      mbar_init(tempty0 + 8 * j, C::EPI_WARPS);  // one arrive per epilogue warp
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -259,7 +278,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
       uint32_t kbg = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
-        const Tile tl = decode_tile(p, tile);
+        const Tile tl = decode_tile<BN>(p, tile);
         for (int kb = 0; kb < nk; kb++, kbg++) {
           const uint32_t s = kbg % STAGES;
           const uint32_t ph = (kbg / STAGES) & 1;
@@ -269,9 +288,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
           const uint32_t dst = smem_u32(smem + s * STAGE_BYTES);
           const int kc = kb * BK;
           tma_load_3d(dst, &p.a_hi, full, kc, tl.m0, tl.bz);
-          tma_load_3d(dst + TILE_BYTES, &p.a_lo, full, kc, tl.m0, tl.bz);
-          tma_load_3d(dst + 2 * TILE_BYTES, &p.b_hi, full, kc, tl.n0, tl.bz);
-          tma_load_3d(dst + 3 * TILE_BYTES, &p.b_lo, full, kc, tl.n0, tl.bz);
+          tma_load_3d(dst + TILE_A, &p.a_lo, full, kc, tl.m0, tl.bz);
+          tma_load_3d(dst + 2 * TILE_A, &p.b_hi, full, kc, tl.n0, tl.bz);
+          tma_load_3d(dst + 2 * TILE_A + TILE_B, &p.b_lo, full, kc, tl.n0, tl.bz);
         }
       }
     }
@@ -295,12 +314,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
 #pragma unroll
             for (int kk = 0; kk < BK / 8; kk++) {
               const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle atom
-              const uint64_t ah = make_desc(base + off), al = make_desc(base + TILE_BYTES + off);
-              const uint64_t bh = make_desc(base + 2 * TILE_BYTES + off), bl = make_desc(base + 3 * TILE_BYTES + off);
+              const uint64_t ah = make_desc(base + off), al = make_desc(base + TILE_A + off);
+              const uint64_t bh = make_desc(base + 2 * TILE_A + off), bl = make_desc(base + 2 * TILE_A + TILE_B + off);
               const uint32_t first = (kb == c * CHUNK_KB && kk == 0) ? 0u : 1u;
-              mma_tf32(dacc, al, bh, first);  // small terms first
-              mma_tf32(dacc, ah, bl, 1u);
-              mma_tf32(dacc, ah, bh, 1u);
+              mma_tf32(dacc, al, bh, C::IDESC, first);  // small terms first
+              mma_tf32(dacc, ah, bl, C::IDESC, 1u);
+              mma_tf32(dacc, ah, bh, C::IDESC, 1u);
             }
             mma_commit(empty0 + 8 * s);
           }
@@ -309,22 +328,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
       }
     }
   } else {
-    // Epilogue warps 2..5: TMEM lane quarter q = warp % 4 holds tile rows 32q..32q+31.
+    // Epilogue warps 2..: TMEM lane quarter q = warp % 4 holds tile rows
+    // 32q..32q+31; warp group h = (warp - 2) / 4 owns columns 128h..128h+127.
     const int q = warp & 3;
+    const int h = (warp - 2) >> 2;
     uint32_t cg = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
-      const Tile tl = decode_tile(p, tile);
-      float acc[BN];
+      const Tile tl = decode_tile<BN>(p, tile);
+      constexpr int EC = 128;  // columns per epilogue warp
+      float acc[EC];
 #pragma unroll
-      for (int i = 0; i < BN; i++) acc[i] = 0.0f;
+      for (int i = 0; i < EC; i++) acc[i] = 0.0f;
       for (int c = 0; c < nchunks; c++, cg++) {
         const uint32_t j = cg % NBUF, use = cg / NBUF;
         bool w = mbar_wait(tfull0 + 8 * j, use & 1, p.err, 3);
         w = __all_sync(0xffffffffu, w);  // tcgen05.ld below is warp-collective
         if (!w) { ok = false; break; }
         tc_fence_after();
-        const uint32_t src = tmem + (uint32_t(32 * q) << 16) + j * BN;
+        const uint32_t src = tmem + (uint32_t(32 * q) << 16) + j * BN + h * EC;
 #pragma unroll
         for (int cc = 0; cc < BN / 32; cc += 2) {
           uint32_t r0[32], r1[32];
@@ -347,13 +369,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
       // block, lanes write their row into a padded shared-memory block, then
       // read it back by column so that every global access (store, bias,
       // residual) is one coalesced 128-byte row segment.
-      float *st = ostage + q * 32 * STAGE_PITCH;
+      float *st = ostage + (warp - 2) * 32 * STAGE_PITCH;
       const int64_t coff = (tl.bz / p.bin) * p.stride_c + (tl.bz % p.bin) * p.stride_c_in;
       float *cbase = p.C + coff;
       const float *res = p.epi.residual ? p.epi.residual + coff : nullptr;
-      const int64_t col = int64_t(tl.n0) + lane;
+      const int64_t col = int64_t(tl.n0) + h * EC + lane;
 #pragma unroll
-      for (int cb = 0; cb < BN / 32; cb++) {
+      for (int cb = 0; cb < EC / 32; cb++) {
 #pragma unroll
         for (int i = 0; i < 32; i++) st[lane * STAGE_PITCH + i] = acc[32 * cb + i];
         __syncwarp();
@@ -432,12 +454,12 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-bool make_map(CUtensorMap *m, const float *base, int64_t Kp, int64_t rows, int64_t batch) {
+bool make_map(CUtensorMap *m, const float *base, int64_t Kp, int64_t rows, int64_t batch, int box_rows = BM) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[3] = {cuuint64_t(Kp), cuuint64_t(rows), cuuint64_t(batch)};
   cuuint64_t strides[2] = {cuuint64_t(Kp) * 4, cuuint64_t(Kp) * 4 * cuuint64_t(rows)};
-  cuuint32_t box[3] = {BK, BM, 1};
+  cuuint32_t box[3] = {BK, cuuint32_t(box_rows), 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -448,6 +470,22 @@ bool make_map(CUtensorMap *m, const float *base, int64_t Kp, int64_t rows, int64
 int64_t padded_k(int64_t K) { return ((K + BK - 1) / BK) * BK; }
 
 }  // namespace
+
+template <int BN>
+silcu_status launch_tc(const TcParams &p, uint32_t grid, cudaStream_t s) {
+  using C = Cfg<BN>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(tc_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return fail(SILCU_CUDA_ERROR, "sgemm(tc): smem attribute: %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  tc_gemm_kernel<BN><<<grid, C::NUM_THREADS, C::SMEM_BYTES, s>>>(p);
+  return check_launch("sgemm(tc)");
+}
 
 int64_t total_batch(const silcu_gemm_args &a) { return a.batch * (a.batch_inner > 1 ? a.batch_inner : 1); }
 
@@ -462,6 +500,7 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
   if (!ws || wsb < need) return fail(SILCU_WORKSPACE_TOO_SMALL, "sgemm(tc): workspace %zu < %zu", wsb, need);
   if (a.M > (1 << 30) || a.N > (1 << 30) || Kp > (1 << 30))
     return fail(SILCU_UNSUPPORTED, "sgemm(tc): extent >= 2^30");
+  const int BN = a.N > 128 ? 256 : 128;  // wide tiles unless N is small
   const int64_t tiles_m = (a.M + BM - 1) / BM, tiles_n = (a.N + BN - 1) / BN;
   const int64_t nb = total_batch(a), bin = a.batch_inner > 1 ? a.batch_inner : 1;
   if (tiles_m * tiles_n * nb > 0x7FFFFFFF) return fail(SILCU_UNSUPPORTED, "sgemm(tc): too many tiles");
@@ -488,7 +527,7 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
   TcParams p;
   memset(&p, 0, sizeof(p));
   if (!make_map(&p.a_hi, a_hi, Kp, a.M, nb) || !make_map(&p.a_lo, a_lo, Kp, a.M, nb) ||
-      !make_map(&p.b_hi, b_hi, Kp, a.N, nb) || !make_map(&p.b_lo, b_lo, Kp, a.N, nb))
+      !make_map(&p.b_hi, b_hi, Kp, a.N, nb, BN) || !make_map(&p.b_lo, b_lo, Kp, a.N, nb, BN))
     return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed");
   p.C = a.C;
   p.ldc = a.ldc;
@@ -515,18 +554,9 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
   p.err = device_error_ptr();
   if (!p.err) return fail(SILCU_CUDA_ERROR, "sgemm(tc): no device error word");
 
-  static bool configured[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e != cudaSuccess) return fail(SILCU_CUDA_ERROR, "sgemm(tc): smem attribute: %s", cudaGetErrorString(e));
-    configured[dev] = true;
-  }
   const int64_t total = tiles_m * tiles_n * nb;
   const uint32_t grid = uint32_t(total < sm_count() ? total : sm_count());
-  tc_gemm_kernel<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(p);
-  return check_launch("sgemm(tc)");
+  return BN == 256 ? launch_tc<256>(p, grid, s) : launch_tc<128>(p, grid, s);
 }
 
 }  // namespace silcu
