@@ -196,6 +196,16 @@ typedef struct silcu_gemm_args {
   const float *residual;  /* NULL, or C += residual[row * ldr + col] after act */
   int64_t ldr;
   int32_t algo;           /* silcu_gemm_algo */
+  /* Optional operands held as an exact tf32 split (x = hi + lo, hi =
+   * tf32_rna(x)), the format the tensor-core path consumes.  A_hi/A_lo: A in
+   * its normal [M,K] layout (lda, A's batch strides; trans_a must be 0).
+   * B_hi/B_lo: B with trans_b = 1 ([N,K], ldb) is read directly; with
+   * trans_b = 0 it is re-split internally.  C_hi/C_lo: also (or only, if C
+   * is NULL) write the split of the result, in C's layout (ldc, strides).
+   * Split arrays need 16-byte aligned rows and batch strides; they select
+   * the tensor-core path. */
+  const float *A_hi, *A_lo, *B_hi, *B_lo;
+  float *C_hi, *C_lo;
 } silcu_gemm_args;
 
 size_t silcu_sgemm_workspace_bytes(const silcu_gemm_args *args_host);

@@ -49,7 +49,8 @@ class GemmArgs(C.Structure):
                 ("batch_inner", i64), ("stride_a_inner", i64), ("stride_b_inner", i64),
                 ("stride_c_inner", i64),
                 ("alpha", f32), ("bias", vp), ("bias_len", i64), ("act", i32),
-                ("residual", vp), ("ldr", i64), ("algo", i32)]
+                ("residual", vp), ("ldr", i64), ("algo", i32),
+                ("A_hi", vp), ("A_lo", vp), ("B_hi", vp), ("B_lo", vp), ("C_hi", vp), ("C_lo", vp)]
 
 
 _SIGS = {

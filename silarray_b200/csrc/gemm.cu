@@ -307,7 +307,12 @@ Epi make_epi(const silcu_gemm_args &a) {
 }
 
 silcu_status validate(const silcu_gemm_args &a) {
-  if (!a.A || !a.B || !a.C) return fail(SILCU_INVALID_ARGUMENT, "sgemm: null pointer");
+  const bool has_a = a.A || (a.A_hi && a.A_lo), has_b = a.B || (a.B_hi && a.B_lo);
+  const bool has_c = a.C || (a.C_hi && a.C_lo);
+  if (!has_a || !has_b || !has_c) return fail(SILCU_INVALID_ARGUMENT, "sgemm: null pointer");
+  const bool any_split = a.A_hi || a.A_lo || a.B_hi || a.B_lo || a.C_hi || a.C_lo;
+  if (any_split && a.algo == SILCU_GEMM_FFMA)
+    return fail(SILCU_UNSUPPORTED, "sgemm: split operands need the tensor-core path");
   if (a.M < 0 || a.N < 0 || a.K < 0 || a.batch < 1 || a.batch_inner < 0)
     return fail(SILCU_INVALID_ARGUMENT, "sgemm: negative extent or batch < 1");
   if (a.bias && a.bias_len <= 0) return fail(SILCU_INVALID_ARGUMENT, "sgemm: bias_len <= 0");
@@ -325,6 +330,7 @@ silcu_status validate(const silcu_gemm_args &a) {
 }  // namespace
 
 int gemm_path(const silcu_gemm_args &a) {
+  if (a.A_hi || a.A_lo || a.B_hi || a.B_lo || a.C_hi || a.C_lo) return kPathTc;
   if (a.algo == SILCU_GEMM_FFMA) return kPathFfma;
   if (a.algo == SILCU_GEMM_TC3XTF32) return kPathTc;
   if (skinny_eligible(a)) return kPathSkinny;

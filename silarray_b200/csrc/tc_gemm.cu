@@ -6,8 +6,10 @@
 // fp32), and  A.B ~= Ah.Bh + Ah.Bl + Al.Bh  accumulated in fp32 in TMEM.
 //
 // Pipeline (persistent: one CTA per SM walks 128x128 output tiles):
-//   pack_split  (pre-pass) writes hi/lo copies of A and B, K-major, K padded
-//               to a multiple of 32, one pass over each operand;
+//   split       operands may arrive already split (hi/lo arrays, K-major,
+//               e.g. written by the producing kernel); otherwise a pre-pass
+//               (pack_split / split_contig) writes hi/lo copies, K-major, K
+//               padded to a multiple of 32;
 //   warp 0      TMA producer: 4 boxes of 128 rows x 32 fp32 (128 B, 128-byte
 //               swizzle) per K block into a 3-stage shared-memory ring;
 //   warp 1      allocates all 512 TMEM columns (4 accumulator buffers of 128),
@@ -33,7 +35,6 @@ namespace silcu {
 namespace {
 
 constexpr int BM = 128, BK = 32;
-constexpr int STAGE_PITCH = 33;  // floats per staged output row (bank-conflict free)
 
 // Per-variant constants: BN = 128 (3-stage ring, 4 TMEM chunk buffers, 4
 // epilogue warps) or BN = 256 (2-stage ring, 2 chunk buffers, 8 epilogue
@@ -48,7 +49,7 @@ struct Cfg {
   static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
   static constexpr int EPI_WARPS = BN / 32;
-  static constexpr int OUT_STAGE_BYTES = EPI_WARPS * 32 * STAGE_PITCH * 4;
+  static constexpr int OUT_STAGE_BYTES = EPI_WARPS * 4096;  // one 32x32 fp32 block per epilogue warp
   static constexpr int SMEM_BYTES = RING_BYTES + OUT_STAGE_BYTES + 1024 + 256;
   static constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int NBUF = 512 / BN;  // TMEM accumulator buffers (chunks in flight)
@@ -65,17 +66,19 @@ constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s per wait
 struct TcEpi {
   float alpha;
   const float *bias;
-  int64_t bias_len;
+  int bias_len;
   int act;
   const float *residual;
   int64_t ldr;
 };
 
 struct __align__(64) TcParams {
-  CUtensorMap a_hi, a_lo, b_hi, b_lo;  // 3-D {Kp, rows, batch}
-  float *C;
-  int64_t ldc, stride_c, bin, stride_c_in;
-  int M, N, Kp, tiles_m, tiles_n, nbatch, chunk_kb;
+  CUtensorMap a_hi, a_lo, b_hi, b_lo;  // 4-D {K, rows, batch_inner, batch}, box {32, 128|BN, 1, 1}
+  CUtensorMap c_map, chi_map, clo_map; // 4-D {N, M, batch_inner, batch}, box {32, 32, 1, 1}
+  float *C;                            // direct-store fallback when C cannot take TMA stores
+  int64_t ldc, stride_c, stride_c_in;
+  int M, N, K, tiles_m, tiles_n, nbatch, bin, chunk_kb;
+  int tma_c, split_out;
   TcEpi epi;
   int *err;
 };
@@ -128,13 +131,34 @@ __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *err, 
   }
 }
 
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0, int c1,
-                                            int c2) {
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0, int c1,
+                                            int c2, int c3) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
+}
+
+// TMA store of one 32x32 fp32 box from shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, uint32_t src, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t h;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+  return __uint_as_float(h);
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -186,27 +210,6 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[3
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-__device__ __forceinline__ float epi_apply(const TcEpi &e, float acc, int64_t row, int64_t col,
-                                           const float *res) {
-  float v = acc;
-  if (e.alpha != 1.0f) v = __fmul_rn(v, e.alpha);
-  if (e.bias) v = __fadd_rn(v, __ldg(e.bias + (col % e.bias_len)));
-  if (e.act == SILCU_ACT_RELU) v = v >= 0.0f ? v : 0.0f;
-  else if (e.act == SILCU_ACT_SIGMOID) v = sigmoid_ref(v);
-  if (res) v = __fadd_rn(v, __ldg(res + row * e.ldr + col));
-  return v;
-}
-
-// ------------------------------------------------------------------- kernel
-// Accumulation is split in two levels (the remedy of Ootomo & Yokota for the
-// tensor core's truncating fp32 accumulation): the MMAs of CHUNK_KB K blocks
-// accumulate into one of two TMEM buffers; the epilogue warps drain each
-// finished chunk into fp32 registers with round-to-nearest adds while the
-// MMAs continue in the other buffer.
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
 struct Tile {
   int bz, m0, n0;
 };
@@ -229,9 +232,39 @@ __device__ __forceinline__ Tile decode_tile(const TcParams &p, int idx) {
   return r;
 }
 
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Writes a lane's 32 values (its row of a 32x32 block) into the warp's 4 KB
+// staging block in the TMA 128-byte-swizzle layout: 16-byte chunk j of row r
+// sits at chunk j ^ (r & 7).  Conflict-free: 8 consecutive lanes cover all banks.
+// mode 0 stores the values, 1 their tf32 hi part, 2 the lo remainder.
+__device__ __forceinline__ float split_part(float x, int mode) {
+  if (mode == 0) return x;
+  const float hi = tf32_rna(x);
+  return mode == 1 ? hi : __fsub_rn(x, hi);
+}
+
+template <int N>
+__device__ __forceinline__ void stage_row_swz(float *st, int lane, const float (&v)[N], int base, int mode) {
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    float4 f = make_float4(split_part(v[base + 4 * j], mode), split_part(v[base + 4 * j + 1], mode),
+                           split_part(v[base + 4 * j + 2], mode), split_part(v[base + 4 * j + 3], mode));
+    *reinterpret_cast<float4 *>(st + lane * 32 + 4 * (j ^ (lane & 7))) = f;
+  }
+}
+
 // Persistent: CTA i takes tiles i, i + gridDim.x, ...  The TMA ring, the MMA
 // chunk buffers and the epilogue run as one continuous stream across tiles,
 // so a tile's pipeline fill and its output store overlap its neighbours'.
+//
+// Accumulation is split in two levels (the remedy of Ootomo & Yokota for the
+// tensor core's truncating fp32 accumulation): the MMAs of chunk_kb K blocks
+// accumulate into one of NBUF TMEM buffers; the epilogue warps drain each
+// finished chunk into fp32 registers with round-to-nearest adds while the
+// MMAs continue in the other buffers.
 template <int BN_>
 __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
   using C = Cfg<BN_>;
@@ -248,7 +281,7 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total_tiles = p.tiles_m * p.tiles_n * p.nbatch;
-  const int nk = p.Kp / BK;
+  const int nk = (p.K + BK - 1) / BK;
   const int CHUNK_KB = p.chunk_kb;
   const int nchunks = (nk + CHUNK_KB - 1) / CHUNK_KB;
 
@@ -279,6 +312,7 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
       bool ok = true;
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         const Tile tl = decode_tile<BN>(p, tile);
+        const int bo = tl.bz / p.bin, bi = tl.bz % p.bin;
         for (int kb = 0; kb < nk; kb++, kbg++) {
           const uint32_t s = kbg % STAGES;
           const uint32_t ph = (kbg / STAGES) & 1;
@@ -287,10 +321,10 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
           mbar_expect_tx(full, STAGE_BYTES);
           const uint32_t dst = smem_u32(smem + s * STAGE_BYTES);
           const int kc = kb * BK;
-          tma_load_3d(dst, &p.a_hi, full, kc, tl.m0, tl.bz);
-          tma_load_3d(dst + TILE_A, &p.a_lo, full, kc, tl.m0, tl.bz);
-          tma_load_3d(dst + 2 * TILE_A, &p.b_hi, full, kc, tl.n0, tl.bz);
-          tma_load_3d(dst + 2 * TILE_A + TILE_B, &p.b_lo, full, kc, tl.n0, tl.bz);
+          tma_load_4d(dst, &p.a_hi, full, kc, tl.m0, bi, bo);
+          tma_load_4d(dst + TILE_A, &p.a_lo, full, kc, tl.m0, bi, bo);
+          tma_load_4d(dst + 2 * TILE_A, &p.b_hi, full, kc, tl.n0, bi, bo);
+          tma_load_4d(dst + 2 * TILE_A + TILE_B, &p.b_lo, full, kc, tl.n0, bi, bo);
         }
       }
     }
@@ -332,6 +366,8 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
     // 32q..32q+31; warp group h = (warp - 2) / 4 owns columns 128h..128h+127.
     const int q = warp & 3;
     const int h = (warp - 2) >> 2;
+    float *st = ostage + (warp - 2) * 1024;
+    const uint32_t st_addr = smem_u32(st);
     uint32_t cg = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
@@ -348,7 +384,7 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
         tc_fence_after();
         const uint32_t src = tmem + (uint32_t(32 * q) << 16) + j * BN + h * EC;
 #pragma unroll
-        for (int cc = 0; cc < BN / 32; cc += 2) {
+        for (int cc = 0; cc < EC / 32; cc += 2) {
           uint32_t r0[32], r1[32];
           tmem_ld32_nowait(src + uint32_t(32 * cc), r0);
           tmem_ld32_nowait(src + uint32_t(32 * cc + 32), r1);
@@ -365,31 +401,91 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
       }
       const bool good = __all_sync(0xffffffffu, ok && *reinterpret_cast<volatile int *>(p.err) == 0);
       if (!good) break;
-      // Store: each warp owns rows 32q..32q+31 of the tile.  Per 32-column
-      // block, lanes write their row into a padded shared-memory block, then
-      // read it back by column so that every global access (store, bias,
-      // residual) is one coalesced 128-byte row segment.
-      float *st = ostage + (warp - 2) * 32 * STAGE_PITCH;
-      const int64_t coff = (tl.bz / p.bin) * p.stride_c + (tl.bz % p.bin) * p.stride_c_in;
-      float *cbase = p.C + coff;
-      const float *res = p.epi.residual ? p.epi.residual + coff : nullptr;
-      const int64_t col = int64_t(tl.n0) + h * EC + lane;
+      // Epilogue math in registers (lane = row): alpha, bias, activation,
+      // residual, in the reference's order; then 32x32 blocks leave through
+      // shared memory (TMA stores, or a transposed coalesced store fallback).
+      const int bo = tl.bz / p.bin, bi = tl.bz % p.bin;
+      const int row = tl.m0 + 32 * q + lane;
+      const int64_t coff = int64_t(bo) * p.stride_c + int64_t(bi) * p.stride_c_in;
 #pragma unroll
       for (int cb = 0; cb < EC / 32; cb++) {
+        const int col0 = tl.n0 + h * EC + 32 * cb;
+        if (col0 >= p.N) break;  // warp-uniform
+        if (p.epi.alpha != 1.0f) {
 #pragma unroll
-        for (int i = 0; i < 32; i++) st[lane * STAGE_PITCH + i] = acc[32 * cb + i];
-        __syncwarp();
-        const int64_t c = col + 32 * cb;
-        if (c < p.N) {
-#pragma unroll 4
-          for (int r = 0; r < 32; r++) {
-            const int64_t row = int64_t(tl.m0) + 32 * q + r;
-            if (row < p.M) cbase[row * p.ldc + c] = epi_apply(p.epi, st[r * STAGE_PITCH + lane], row, c, res);
+          for (int i = 0; i < 32; i++) acc[32 * cb + i] = __fmul_rn(acc[32 * cb + i], p.epi.alpha);
+        }
+        if (p.epi.bias) {
+          int bix = col0 % p.epi.bias_len;
+#pragma unroll
+          for (int i = 0; i < 32; i++) {
+            acc[32 * cb + i] = __fadd_rn(acc[32 * cb + i], __ldg(p.epi.bias + bix));
+            if (++bix == p.epi.bias_len) bix = 0;
           }
         }
-        __syncwarp();
+        if (p.epi.act == SILCU_ACT_RELU) {
+#pragma unroll
+          for (int i = 0; i < 32; i++) acc[32 * cb + i] = acc[32 * cb + i] >= 0.0f ? acc[32 * cb + i] : 0.0f;
+        } else if (p.epi.act == SILCU_ACT_SIGMOID) {
+#pragma unroll
+          for (int i = 0; i < 32; i++) acc[32 * cb + i] = sigmoid_ref(acc[32 * cb + i]);
+        }
+        if (p.epi.residual && row < p.M) {
+          const float *rp = p.epi.residual + coff + int64_t(row) * p.epi.ldr + col0;
+          if (col0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(rp) & 15) == 0)) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              const float4 r4 = __ldg(reinterpret_cast<const float4 *>(rp + i));
+              acc[32 * cb + i] = __fadd_rn(acc[32 * cb + i], r4.x);
+              acc[32 * cb + i + 1] = __fadd_rn(acc[32 * cb + i + 1], r4.y);
+              acc[32 * cb + i + 2] = __fadd_rn(acc[32 * cb + i + 2], r4.z);
+              acc[32 * cb + i + 3] = __fadd_rn(acc[32 * cb + i + 3], r4.w);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; i++)
+              if (col0 + i < p.N) acc[32 * cb + i] = __fadd_rn(acc[32 * cb + i], __ldg(rp + i));
+          }
+        }
+        if (p.tma_c || p.split_out) {
+          // up to three outputs leave through the one staging block
+#pragma unroll 1
+          for (int o = 0; o < 3; o++) {
+            if (o == 0 && !p.tma_c) continue;
+            if (o > 0 && !p.split_out) break;
+            if (lane == 0) bulk_wait_read0();  // the previous store has read the block
+            __syncwarp();
+            stage_row_swz(st, lane, acc, 32 * cb, o);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              const CUtensorMap *m = o == 0 ? &p.c_map : (o == 1 ? &p.chi_map : &p.clo_map);
+              tma_store_4d(m, st_addr, col0, tl.m0 + 32 * q, bi, bo);
+              bulk_commit();
+            }
+          }
+        } else {
+          // Fallback (C not TMA-compatible): transpose through the staging
+          // block (XOR-swizzled columns, conflict-free) and store 128-byte
+          // row segments.
+#pragma unroll
+          for (int i = 0; i < 32; i++) st[lane * 32 + (i ^ lane)] = acc[32 * cb + i];
+          __syncwarp();
+          const int c = col0 + lane;
+          if (c < p.N) {
+            float *cp = p.C + coff + c;
+#pragma unroll 4
+            for (int r = 0; r < 32; r++) {
+              const int rr = tl.m0 + 32 * q + r;
+              if (rr < p.M) cp[int64_t(rr) * p.ldc] = st[r * 32 + (lane ^ r)];
+            }
+          }
+          __syncwarp();
+        }
       }
     }
+    if (lane == 0) bulk_wait_all0();  // every TMA store has completed before exit
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -401,25 +497,39 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
 
 // ----------------------------------------------------------- split pre-pass
 // src element (b, r, k) at src + (b / bin)*sbatch + (b % bin)*sbatch_in + r*rs + k*ks
-// (one of rs/ks is 1).  Writes hi/lo[(b*rows + r)*Kp + k]; k in [K, Kp) is zero-filled.
-__global__ void __launch_bounds__(256) pack_split(const float *__restrict__ src, int64_t rs, int64_t ks,
-                                                  int64_t sbatch, int64_t bin, int64_t sbatch_in,
-                                                  int64_t rows, int64_t K, int64_t Kp,
+// (one of rs/ks is 1); when src_lo is given the value is src + src_lo (an
+// operand already held as an exact hi/lo pair).  Writes hi/lo[(b*rows + r)*Kp + k];
+// k in [K, Kp) is zero-filled.
+__global__ void __launch_bounds__(256) pack_split(const float *__restrict__ src, const float *__restrict__ src_lo,
+                                                  int64_t rs, int64_t ks, int64_t sbatch, int64_t bin,
+                                                  int64_t sbatch_in, int64_t rows, int64_t K, int64_t Kp,
                                                   float *__restrict__ hi, float *__restrict__ lo) {
   __shared__ float tile[32][33];
   const int64_t b = blockIdx.z;
   const int64_t r0 = int64_t(blockIdx.y) * 32, k0 = int64_t(blockIdx.x) * 32;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
-  const float *s = src + (b / bin) * sbatch + (b % bin) * sbatch_in;
+  const int64_t boff = (b / bin) * sbatch + (b % bin) * sbatch_in;
+  const float *s = src + boff;
+  const float *sl = src_lo ? src_lo + boff : nullptr;
   if (ks == 1) {  // k contiguous: read along k
     for (int i = ty; i < 32; i += 8) {
       const int64_t r = r0 + i, k = k0 + tx;
-      tile[i][tx] = (r < rows && k < K) ? __ldg(s + r * rs + k) : 0.0f;
+      float x = 0.0f;
+      if (r < rows && k < K) {
+        x = __ldg(s + r * rs + k);
+        if (sl) x = __fadd_rn(x, __ldg(sl + r * rs + k));
+      }
+      tile[i][tx] = x;
     }
   } else {  // r contiguous: read along r, transpose through shared memory
     for (int i = ty; i < 32; i += 8) {
       const int64_t k = k0 + i, r = r0 + tx;
-      tile[tx][i] = (r < rows && k < K) ? __ldg(s + r * rs + k * ks) : 0.0f;
+      float x = 0.0f;
+      if (r < rows && k < K) {
+        x = __ldg(s + r * rs + k * ks);
+        if (sl) x = __fadd_rn(x, __ldg(sl + r * rs + k * ks));
+      }
+      tile[tx][i] = x;
     }
   }
   __syncthreads();
@@ -427,12 +537,35 @@ __global__ void __launch_bounds__(256) pack_split(const float *__restrict__ src,
     const int64_t r = r0 + i, k = k0 + tx;
     if (r < rows && k < Kp) {
       const float x = tile[i][tx];
-      uint32_t h;
-      asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
-      const float xh = __uint_as_float(h);
+      const float xh = tf32_rna(x);
       const size_t o = size_t(b * rows + r) * size_t(Kp) + size_t(k);
       hi[o] = xh;
       lo[o] = __fsub_rn(x, xh);
+    }
+  }
+}
+
+// Elementwise split of a contiguous K-major operand (no transposition):
+// 4 elements per thread, 128-bit loads and stores.
+__global__ void __launch_bounds__(256) split_contig(const float *__restrict__ src, uint64_t n,
+                                                    float *__restrict__ hi, float *__restrict__ lo) {
+  const uint64_t stride = uint64_t(gridDim.x) * 256 * 4;
+  for (uint64_t i = (uint64_t(blockIdx.x) * 256 + threadIdx.x) * 4; i < n; i += stride) {
+    if (i + 4 <= n) {
+      const float4 x = __ldcs(reinterpret_cast<const float4 *>(src + i));
+      float4 a, b;
+      a.x = tf32_rna(x.x); b.x = __fsub_rn(x.x, a.x);
+      a.y = tf32_rna(x.y); b.y = __fsub_rn(x.y, a.y);
+      a.z = tf32_rna(x.z); b.z = __fsub_rn(x.z, a.z);
+      a.w = tf32_rna(x.w); b.w = __fsub_rn(x.w, a.w);
+      *reinterpret_cast<float4 *>(hi + i) = a;
+      *reinterpret_cast<float4 *>(lo + i) = b;
+    } else {
+      for (uint64_t k = i; k < n; k++) {
+        const float x = src[k], xh = tf32_rna(x);
+        hi[k] = xh;
+        lo[k] = __fsub_rn(x, xh);
+      }
     }
   }
 }
@@ -454,22 +587,31 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-bool make_map(CUtensorMap *m, const float *base, int64_t Kp, int64_t rows, int64_t batch, int box_rows = BM) {
+// A 4-D fp32 view {inner, rows, bin, bout} with element strides {1, ld, s_in,
+// s_out}, boxes {box0, box1, 1, 1}, 128-byte swizzle.  Strides of extent-1
+// dimensions are replaced by a valid dummy.
+bool make_map4(CUtensorMap *m, const float *base, int64_t inner, int64_t rows, int64_t ld, int64_t bin,
+               int64_t s_in, int64_t bout, int64_t s_out, int box0, int box1) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
-  cuuint64_t dims[3] = {cuuint64_t(Kp), cuuint64_t(rows), cuuint64_t(batch)};
-  cuuint64_t strides[2] = {cuuint64_t(Kp) * 4, cuuint64_t(Kp) * 4 * cuuint64_t(rows)};
-  cuuint32_t box[3] = {BK, cuuint32_t(box_rows), 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box, estr,
+  const int64_t span = ld * rows;
+  if (bin <= 1) s_in = span;
+  if (bout <= 1) s_out = s_in * (bin > 1 ? bin : 1);
+  cuuint64_t dims[4] = {cuuint64_t(inner), cuuint64_t(rows), cuuint64_t(bin), cuuint64_t(bout)};
+  cuuint64_t strides[3] = {cuuint64_t(ld) * 4, cuuint64_t(s_in) * 4, cuuint64_t(s_out) * 4};
+  cuuint32_t box[4] = {cuuint32_t(box0), cuuint32_t(box1), 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float *>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
-int64_t padded_k(int64_t K) { return ((K + BK - 1) / BK) * BK; }
+bool aligned_view(const void *p, int64_t ld, int64_t s_in, int64_t s_out) {
+  return p && aligned16(p) && ld % 4 == 0 && s_in % 4 == 0 && s_out % 4 == 0 && ld > 0;
+}
 
-}  // namespace
+int64_t padded_k(int64_t K) { return ((K + BK - 1) / BK) * BK; }
 
 template <int BN>
 silcu_status launch_tc(const TcParams &p, uint32_t grid, cudaStream_t s) {
@@ -487,59 +629,120 @@ silcu_status launch_tc(const TcParams &p, uint32_t grid, cudaStream_t s) {
   return check_launch("sgemm(tc)");
 }
 
+bool a_given_split(const silcu_gemm_args &a) { return a.A_hi && a.A_lo; }
+bool b_given_split_kmajor(const silcu_gemm_args &a) { return a.B_hi && a.B_lo && a.trans_b; }
+
+}  // namespace
+
 int64_t total_batch(const silcu_gemm_args &a) { return a.batch * (a.batch_inner > 1 ? a.batch_inner : 1); }
 
 size_t tc_workspace_bytes(const silcu_gemm_args &a) {
   const int64_t Kp = padded_k(a.K > 0 ? a.K : 1);
-  return size_t(2) * size_t(Kp) * size_t(total_batch(a)) * size_t(a.M + a.N) * sizeof(float) + 256;
+  size_t bytes = 256;
+  if (!a_given_split(a)) bytes += size_t(2) * Kp * size_t(total_batch(a)) * size_t(a.M) * sizeof(float);
+  if (!b_given_split_kmajor(a)) bytes += size_t(2) * Kp * size_t(total_batch(a)) * size_t(a.N) * sizeof(float);
+  return bytes;
 }
 
 silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t s) {
   const int64_t Kp = padded_k(a.K > 0 ? a.K : 1);
   const size_t need = tc_workspace_bytes(a);
-  if (!ws || wsb < need) return fail(SILCU_WORKSPACE_TOO_SMALL, "sgemm(tc): workspace %zu < %zu", wsb, need);
+  if (need > 256 && (!ws || wsb < need))
+    return fail(SILCU_WORKSPACE_TOO_SMALL, "sgemm(tc): workspace %zu < %zu", wsb, need);
   if (a.M > (1 << 30) || a.N > (1 << 30) || Kp > (1 << 30))
     return fail(SILCU_UNSUPPORTED, "sgemm(tc): extent >= 2^30");
   const int BN = a.N > 128 ? 256 : 128;  // wide tiles unless N is small
   const int64_t tiles_m = (a.M + BM - 1) / BM, tiles_n = (a.N + BN - 1) / BN;
-  const int64_t nb = total_batch(a), bin = a.batch_inner > 1 ? a.batch_inner : 1;
+  const int64_t nb = total_batch(a), bin = a.batch_inner > 1 ? a.batch_inner : 1, bout = a.batch;
   if (tiles_m * tiles_n * nb > 0x7FFFFFFF) return fail(SILCU_UNSUPPORTED, "sgemm(tc): too many tiles");
   if (nb > 65535) return fail(SILCU_UNSUPPORTED, "sgemm(tc): batch > 65535");
-  float *base = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(ws) + 255) & ~uintptr_t(255));
-  const size_t a_elems = size_t(nb) * a.M * Kp, b_elems = size_t(nb) * a.N * Kp;
-  float *a_hi = base, *a_lo = a_hi + a_elems, *b_hi = a_lo + a_elems, *b_lo = b_hi + b_elems;
+  const bool asplit = a_given_split(a), bsplit = b_given_split_kmajor(a);
+  if (a.A_hi && a.trans_a) return fail(SILCU_UNSUPPORTED, "sgemm(tc): split A must be K-major (trans_a = 0)");
+  if (asplit && !(aligned_view(a.A_hi, a.lda, a.stride_a_inner, a.stride_a) &&
+                  aligned_view(a.A_lo, a.lda, a.stride_a_inner, a.stride_a)))
+    return fail(SILCU_INVALID_ARGUMENT, "sgemm(tc): split A needs 16-byte aligned rows and batch strides");
+  if (bsplit && !(aligned_view(a.B_hi, a.ldb, a.stride_b_inner, a.stride_b) &&
+                  aligned_view(a.B_lo, a.ldb, a.stride_b_inner, a.stride_b)))
+    return fail(SILCU_INVALID_ARGUMENT, "sgemm(tc): split B needs 16-byte aligned rows and batch strides");
+  const bool split_out = a.C_hi && a.C_lo;
+  const bool tma_c = a.C && aligned_view(a.C, a.ldc, a.stride_c_inner, a.stride_c);
+  if (split_out && !(aligned_view(a.C_hi, a.ldc, a.stride_c_inner, a.stride_c) &&
+                     aligned_view(a.C_lo, a.ldc, a.stride_c_inner, a.stride_c)))
+    return fail(SILCU_INVALID_ARGUMENT, "sgemm(tc): split output needs 16-byte aligned rows and batch strides");
+  if (!a.C && !split_out) return fail(SILCU_INVALID_ARGUMENT, "sgemm(tc): no output");
 
-  // A: rows m, k.  Non-transposed: (m, k) at m*lda + k.  Transposed: k*lda + m.
-  {
-    const int64_t rs = a.trans_a ? 1 : a.lda, ks = a.trans_a ? a.lda : 1;
-    dim3 g(uint32_t(Kp / 32), uint32_t((a.M + 31) / 32), uint32_t(nb));
-    pack_split<<<g, 256, 0, s>>>(a.A, rs, ks, a.stride_a, bin, a.stride_a_inner, a.M, a.K, Kp, a_hi, a_lo);
-  }
-  // B as rows n, k.  Non-transposed B [K,N]: (n, k) at k*ldb + n.  Transposed [N,K]: n*ldb + k.
-  {
-    const int64_t rs = a.trans_b ? a.ldb : 1, ks = a.trans_b ? 1 : a.ldb;
-    dim3 g(uint32_t(Kp / 32), uint32_t((a.N + 31) / 32), uint32_t(nb));
-    pack_split<<<g, 256, 0, s>>>(a.B, rs, ks, a.stride_b, bin, a.stride_b_inner, a.N, a.K, Kp, b_hi, b_lo);
-  }
-  silcu_status st = check_launch("sgemm(tc) pack", 2);
-  if (st != SILCU_OK) return st;
-
+  float *cur = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(ws) + 255) & ~uintptr_t(255));
   TcParams p;
   memset(&p, 0, sizeof(p));
-  if (!make_map(&p.a_hi, a_hi, Kp, a.M, nb) || !make_map(&p.a_lo, a_lo, Kp, a.M, nb) ||
-      !make_map(&p.b_hi, b_hi, Kp, a.N, nb, BN) || !make_map(&p.b_lo, b_lo, Kp, a.N, nb, BN))
-    return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed");
+  int launches = 0;
+  // A as rows m, K-major.
+  if (asplit) {
+    if (!make_map4(&p.a_hi, a.A_hi, a.K, a.M, a.lda, bin, a.stride_a_inner, bout, a.stride_a, BK, BM) ||
+        !make_map4(&p.a_lo, a.A_lo, a.K, a.M, a.lda, bin, a.stride_a_inner, bout, a.stride_a, BK, BM))
+      return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed (A)");
+  } else {
+    const size_t el = size_t(nb) * a.M * Kp;
+    float *hi = cur, *lo = cur + el;
+    cur += 2 * el;
+    const float *src = a.A ? a.A : a.A_hi;
+    const float *src_lo = a.A ? nullptr : a.A_lo;
+    const int64_t rs = a.trans_a ? 1 : a.lda, ks = a.trans_a ? a.lda : 1;
+    if (!a.trans_a && !src_lo && Kp == a.K && a.lda == a.K && bin == 1 && a.stride_a == a.M * a.K) {
+      const uint64_t n = uint64_t(el);
+      uint64_t g = (n / 4 + 255) / 256;
+      const uint64_t cap = uint64_t(sm_count()) * 8;
+      split_contig<<<uint32_t(g < cap ? (g ? g : 1) : cap), 256, 0, s>>>(src, n, hi, lo);
+    } else {
+      dim3 g(uint32_t(Kp / 32), uint32_t((a.M + 31) / 32), uint32_t(nb));
+      pack_split<<<g, 256, 0, s>>>(src, src_lo, rs, ks, a.stride_a, bin, a.stride_a_inner, a.M, a.K, Kp, hi, lo);
+    }
+    launches++;
+    if (!make_map4(&p.a_hi, hi, Kp, a.M, Kp, bin, a.M * Kp, bout, bin * a.M * Kp, BK, BM) ||
+        !make_map4(&p.a_lo, lo, Kp, a.M, Kp, bin, a.M * Kp, bout, bin * a.M * Kp, BK, BM))
+      return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed (A pack)");
+  }
+  // B as rows n, K-major.  Non-transposed B [K,N]: (n, k) at k*ldb + n.  Transposed [N,K]: n*ldb + k.
+  if (bsplit) {
+    if (!make_map4(&p.b_hi, a.B_hi, a.K, a.N, a.ldb, bin, a.stride_b_inner, bout, a.stride_b, BK, BN) ||
+        !make_map4(&p.b_lo, a.B_lo, a.K, a.N, a.ldb, bin, a.stride_b_inner, bout, a.stride_b, BK, BN))
+      return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed (B)");
+  } else {
+    const size_t el = size_t(nb) * a.N * Kp;
+    float *hi = cur, *lo = cur + el;
+    cur += 2 * el;
+    const float *src = a.B ? a.B : a.B_hi;
+    const float *src_lo = a.B ? nullptr : a.B_lo;
+    const int64_t rs = a.trans_b ? a.ldb : 1, ks = a.trans_b ? 1 : a.ldb;
+    dim3 g(uint32_t(Kp / 32), uint32_t((a.N + 31) / 32), uint32_t(nb));
+    pack_split<<<g, 256, 0, s>>>(src, src_lo, rs, ks, a.stride_b, bin, a.stride_b_inner, a.N, a.K, Kp, hi, lo);
+    launches++;
+    if (!make_map4(&p.b_hi, hi, Kp, a.N, Kp, bin, a.N * Kp, bout, bin * a.N * Kp, BK, BN) ||
+        !make_map4(&p.b_lo, lo, Kp, a.N, Kp, bin, a.N * Kp, bout, bin * a.N * Kp, BK, BN))
+      return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed (B pack)");
+  }
+  if (launches) {
+    silcu_status st = check_launch("sgemm(tc) pack", launches);
+    if (st != SILCU_OK) return st;
+  }
+  if (tma_c && !make_map4(&p.c_map, a.C, a.N, a.M, a.ldc, bin, a.stride_c_inner, bout, a.stride_c, 32, 32))
+    return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed (C)");
+  if (split_out &&
+      (!make_map4(&p.chi_map, a.C_hi, a.N, a.M, a.ldc, bin, a.stride_c_inner, bout, a.stride_c, 32, 32) ||
+       !make_map4(&p.clo_map, a.C_lo, a.N, a.M, a.ldc, bin, a.stride_c_inner, bout, a.stride_c, 32, 32)))
+    return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed (split C)");
   p.C = a.C;
   p.ldc = a.ldc;
   p.stride_c = a.stride_c;
-  p.bin = bin;
   p.stride_c_in = a.stride_c_inner;
+  p.bin = int(bin);
   p.M = int(a.M);
   p.N = int(a.N);
-  p.Kp = int(Kp);
+  p.K = int(Kp);  // K blocks past K read zeros (TMA fill or packed padding)
   p.tiles_m = int(tiles_m);
   p.tiles_n = int(tiles_n);
   p.nbatch = int(nb);
+  p.tma_c = tma_c ? 1 : 0;
+  p.split_out = split_out ? 1 : 0;
   p.chunk_kb = CHUNK_KB_DEFAULT;
   if (const char *env = getenv("SILCU_TC_CHUNK_KB")) {  // tuning knob: K blocks per accumulation chunk
     const int v = atoi(env);
@@ -547,13 +750,12 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
   }
   p.epi.alpha = a.alpha;
   p.epi.bias = a.bias;
-  p.epi.bias_len = a.bias_len > 0 ? a.bias_len : 1;
+  p.epi.bias_len = int(a.bias_len > 0 ? a.bias_len : 1);
   p.epi.act = a.act;
   p.epi.residual = a.residual;
   p.epi.ldr = a.ldr;
   p.err = device_error_ptr();
   if (!p.err) return fail(SILCU_CUDA_ERROR, "sgemm(tc): no device error word");
-
   const int64_t total = tiles_m * tiles_n * nb;
   const uint32_t grid = uint32_t(total < sm_count() ? total : sm_count());
   return BN == 256 ? launch_tc<256>(p, grid, s) : launch_tc<128>(p, grid, s);

@@ -258,18 +258,38 @@ ACT = {None: 0, "none": 0, "relu": 1, "sigmoid": 2}
 def gemm(A, B, C=None, *, M, N, K, lda=None, ldb=None, ldc=None, trans_a=False, trans_b=False,
          batch=1, stride_a=0, stride_b=0, stride_c=0, batch_inner=1, stride_a_inner=0,
          stride_b_inner=0, stride_c_inner=0, alpha=1.0, bias=None, act=None,
-         residual=None, ldr=None, algo="auto"):
-    """C = act(alpha * op(A).op(B) + bias) + residual (silcu_sgemm_ex)."""
-    _dev(A, _F32), _dev(B, _F32)
-    if C is None:
-        C = torch.empty(batch * batch_inner * M * N, dtype=_F32, device=A.device)
+         residual=None, ldr=None, algo="auto", C_split=None, no_c=False):
+    """C = act(alpha * op(A).op(B) + bias) + residual (silcu_sgemm_ex).
+
+    A and B are CUDA float tensors, or (hi, lo) pairs holding the exact tf32
+    split of the operand (what the tensor-core path consumes; written by
+    producers with a split output).  C_split=(hi, lo) additionally writes the
+    split of the result; no_c=True writes only the split."""
+    def ops(X):
+        if isinstance(X, (tuple, list)):
+            _dev(X[0], _F32), _dev(X[1], _F32)
+            return None, X[0], X[1]
+        _dev(X, _F32)
+        return X, None, None
+    Ad, Ah, Al = ops(A)
+    Bd, Bh, Bl = ops(B)
+    dev = (Ad if Ad is not None else Ah).device
+    if C is None and not no_c:
+        C = torch.empty(batch * batch_inner * M * N, dtype=_F32, device=dev)
         if batch_inner > 1 and stride_c_inner == 0:
             stride_c_inner = M * N
         if batch > 1 and stride_c == 0:
             stride_c = batch_inner * M * N
-    _dev(C, _F32)
     a = _lib.GemmArgs()
-    a.A, a.B, a.C = A.data_ptr(), B.data_ptr(), C.data_ptr()
+    ptr = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
+    a.A, a.B = ptr(Ad), ptr(Bd)
+    a.A_hi, a.A_lo, a.B_hi, a.B_lo = ptr(Ah), ptr(Al), ptr(Bh), ptr(Bl)
+    if C is not None:
+        _dev(C, _F32)
+        a.C = C.data_ptr()
+    if C_split is not None:
+        _dev(C_split[0], _F32), _dev(C_split[1], _F32)
+        a.C_hi, a.C_lo = C_split[0].data_ptr(), C_split[1].data_ptr()
     a.M, a.N, a.K = M, N, K
     a.lda = lda if lda is not None else (M if trans_a else K)
     a.ldb = ldb if ldb is not None else (K if trans_b else N)
@@ -290,7 +310,7 @@ def gemm(A, B, C=None, *, M, N, K, lda=None, ldb=None, ldc=None, trans_a=False, 
         a.ldr = ldr if ldr is not None else N
     a.algo = ALGO[algo]
     need = lib().silcu_sgemm_workspace_bytes(ct.byref(a))
-    wp, wn = _ws_args(need, A.device)
+    wp, wn = _ws_args(need, dev)
     check(lib().silcu_sgemm_ex(ct.byref(a), wp, wn, _stream()))
     return C
 

@@ -115,3 +115,35 @@ def test_tc_large_sampled_rows(cuda):
     ref = a[rows].astype(np.float64) @ b.astype(np.float64)
     assert_dot_close(got[rows], ref, n, what="tc 2048 sampled")
     gpu.device_status()
+
+
+def _split(x):
+    """Exact tf32 split of a float32 array (hi = round-to-nearest-away tf32)."""
+    u = x.view(np.uint32).astype(np.uint64)
+    hi = ((u + 0x1000) & 0xFFFFE000).astype(np.uint32).view(np.float32)
+    return hi, (x - hi).astype(np.float32)
+
+
+def test_split_operands_and_split_output(cuda):
+    """Operands given as hi/lo pairs (A K-major, B as [N,K] and as [K,N]) and
+    the split output equal the plain fp32 call bit for bit."""
+    rng = np.random.default_rng(12)
+    M, N, K = 300, 520, 200
+    a = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    bt = rng.uniform(-1, 1, (N, K)).astype(np.float32)
+    ah, al = _split(a)
+    bh, bl = _split(bt)
+    ref = host(gpu.gemm(dev(a), dev(bt), M=M, N=N, K=K, trans_b=True, algo="tc"))
+    hi = torch.empty(M * N, device="cuda")
+    lo = torch.empty(M * N, device="cuda")
+    got = host(gpu.gemm((dev(ah), dev(al)), (dev(bh), dev(bl)), M=M, N=N, K=K, trans_b=True, C_split=(hi, lo)))
+    np.testing.assert_array_equal(got, ref)
+    np.testing.assert_array_equal(host(hi) + host(lo), ref)
+    eh, el = _split(ref)
+    np.testing.assert_array_equal(host(hi), eh)
+    np.testing.assert_array_equal(host(lo), el)
+    b = np.ascontiguousarray(bt.T)
+    b_h, b_l = _split(b)
+    got2 = host(gpu.gemm((dev(ah), dev(al)), (dev(b_h), dev(b_l)), M=M, N=N, K=K))
+    np.testing.assert_array_equal(got2, ref)
+    assert_dot_close(ref.reshape(M, N), O.sgemm(a, bt, tb=True), K, what="split")
