@@ -148,6 +148,14 @@ silcu_status silcu_argmax_all_f32(const float *in, size_t n, int64_t *out_index,
 silcu_status silcu_softmax_f32(const float *in, float *out, size_t rows, size_t cols, silcu_stream stream);
 silcu_status silcu_layer_norm_f32(const float *in, float *out, const float *gamma, const float *beta,
                                   size_t rows, size_t cols, float eps, silcu_stream stream);
+/* The same two ops writing the exact tf32 split of their result: out_hi =
+ * tf32_rna(y), out_lo = y - out_hi (so out_hi + out_lo == y), the operand
+ * format of the tensor-core GEMM (silcu_gemm_args.A_hi/A_lo).  No reference
+ * counterpart: a fusion of gpu::layer_norm/softmax with the GEMM's split. */
+silcu_status silcu_softmax_split_f32(const float *in, float *out_hi, float *out_lo, size_t rows, size_t cols,
+                                     silcu_stream stream);
+silcu_status silcu_layer_norm_split_f32(const float *in, float *out_hi, float *out_lo, const float *gamma,
+                                        const float *beta, size_t rows, size_t cols, float eps, silcu_stream stream);
 silcu_status silcu_argmax_f32(const float *in, int32_t *out, size_t rows, size_t cols,
                               void *workspace, size_t workspace_bytes, silcu_stream stream);
 size_t silcu_argmax_workspace_bytes(size_t rows, size_t cols);
@@ -207,6 +215,13 @@ typedef struct silcu_gemm_args {
   const float *A_hi, *A_lo, *B_hi, *B_lo;
   float *C_hi, *C_lo;
 } silcu_gemm_args;
+
+/* Exact tf32 split of a [rows, cols] fp32 matrix (row stride ld) into
+ * contiguous hi/lo arrays, [rows, cols] or, when transpose, [cols, rows] --
+ * how a constant weight W[K,N] is turned once into the K-major B_hi/B_lo
+ * (trans_b = 1) operand of silcu_sgemm_ex.  No reference counterpart. */
+silcu_status silcu_split_f32(const float *src, size_t rows, size_t cols, size_t ld, int transpose, float *hi,
+                             float *lo, silcu_stream stream);
 
 size_t silcu_sgemm_workspace_bytes(const silcu_gemm_args *args_host);
 silcu_status silcu_sgemm_ex(const silcu_gemm_args *args_host, void *workspace, size_t workspace_bytes,

@@ -75,6 +75,9 @@ _SIGS = {
     "silcu_softmax_f32": ([vp, vp, sz, sz, vp], C.c_int),
     "silcu_layer_norm_f32": ([vp, vp, vp, vp, sz, sz, f32, vp], C.c_int),
     "silcu_argmax_f32": ([vp, vp, sz, sz, vp, sz, vp], C.c_int),
+    "silcu_softmax_split_f32": ([vp, vp, vp, sz, sz, vp], C.c_int),
+    "silcu_layer_norm_split_f32": ([vp, vp, vp, vp, vp, sz, sz, f32, vp], C.c_int),
+    "silcu_split_f32": ([vp, sz, sz, sz, C.c_int, vp, vp, vp], C.c_int),
     "silcu_argmax_workspace_bytes": ([sz, sz], sz),
     "silcu_sum_axis_workspace_bytes": ([sz, sz, sz], sz),
     "silcu_sum_axis_f32": ([vp, vp, sz, sz, sz, vp, sz, vp], C.c_int),

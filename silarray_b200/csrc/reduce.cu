@@ -219,11 +219,42 @@ enum RowOp { kSoftmax = 0, kLayerNorm = 1, kRowArgmax = 2 };
 struct RowArgs {
   const float *in;
   float *out;
+  float *out_lo;  // when set, out / out_lo receive the exact tf32 split (hi, lo) of the result
   int32_t *idx;
   const float *gamma, *beta;
   uint32_t rows, cols;
   float eps;
 };
+
+__device__ __forceinline__ float tf32_hi(float x) {
+  uint32_t h;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+  return __uint_as_float(h);
+}
+
+// Stores four results of row `row`, float4 index c: plain, or split into
+// hi/lo for a consumer on the tensor cores.
+__device__ __forceinline__ void row_store4(const RowArgs &a, uint32_t row, uint32_t c, float4 o) {
+  float4 *dst = reinterpret_cast<float4 *>(a.out + size_t(row) * a.cols);
+  if (!a.out_lo) {
+    __stcs(dst + c, o);
+    return;
+  }
+  float4 h = make_float4(tf32_hi(o.x), tf32_hi(o.y), tf32_hi(o.z), tf32_hi(o.w));
+  float4 l = make_float4(__fsub_rn(o.x, h.x), __fsub_rn(o.y, h.y), __fsub_rn(o.z, h.z), __fsub_rn(o.w, h.w));
+  __stcs(dst + c, h);
+  __stcs(reinterpret_cast<float4 *>(a.out_lo + size_t(row) * a.cols) + c, l);
+}
+
+__device__ __forceinline__ void row_store1(const RowArgs &a, size_t i, float o) {
+  if (!a.out_lo) {
+    a.out[i] = o;
+    return;
+  }
+  const float h = tf32_hi(o);
+  a.out[i] = h;
+  a.out_lo[i] = __fsub_rn(o, h);
+}
 
 // The row cached in registers: VPT float4 per thread.  WARP: one warp per
 // row, 8 rows per CTA of 256 threads (short rows, shuffle-only reductions);
@@ -264,13 +295,12 @@ __global__ void __launch_bounds__(WARP ? 256 : NT) row_kernel(const RowArgs a) {
       }
       s = row_reduce<NT, WARP>(s, sf, Add());
       const float inv = __frcp_rn(s);
-      float4 *dst = reinterpret_cast<float4 *>(a.out + size_t(row) * a.cols);
 #pragma unroll
       for (int j = 0; j < VPT; j++) {
         const uint32_t c = t + j * NT;
         if (c < c4)
-          __stcs(dst + c, make_float4(__fmul_rn(v[j].x, inv), __fmul_rn(v[j].y, inv),
-                                      __fmul_rn(v[j].z, inv), __fmul_rn(v[j].w, inv)));
+          row_store4(a, row, c, make_float4(__fmul_rn(v[j].x, inv), __fmul_rn(v[j].y, inv),
+                                            __fmul_rn(v[j].z, inv), __fmul_rn(v[j].w, inv)));
       }
     } else if (OP == kLayerNorm) {
       float s = 0.f;
@@ -292,7 +322,6 @@ __global__ void __launch_bounds__(WARP ? 256 : NT) row_kernel(const RowArgs a) {
       }
       ss = row_reduce<NT, WARP>(ss, sf, Add());
       const float inv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(a.cols)), a.eps)));
-      float4 *dst = reinterpret_cast<float4 *>(a.out + size_t(row) * a.cols);
       const float4 *g4 = reinterpret_cast<const float4 *>(a.gamma);
       const float4 *b4 = reinterpret_cast<const float4 *>(a.beta);
 #pragma unroll
@@ -305,7 +334,7 @@ __global__ void __launch_bounds__(WARP ? 256 : NT) row_kernel(const RowArgs a) {
           o.y = __fadd_rn(__fmul_rn(__fmul_rn(v[j].y, inv), g.y), b.y);
           o.z = __fadd_rn(__fmul_rn(__fmul_rn(v[j].z, inv), g.z), b.z);
           o.w = __fadd_rn(__fmul_rn(__fmul_rn(v[j].w, inv), g.w), b.w);
-          __stcs(dst + c, o);
+          row_store4(a, row, c, o);
         }
       }
     } else {  // argmax
@@ -348,7 +377,8 @@ __global__ void __launch_bounds__(512) row_kernel_generic(const RowArgs a) {
       for (uint32_t c = t; c < a.cols; c += NT) s += expf(__fsub_rn(src[c], m));
       s = block_reduce<NT>(s, sf, Add());
       const float inv = __frcp_rn(s);
-      for (uint32_t c = t; c < a.cols; c += NT) dst[c] = __fmul_rn(expf(__fsub_rn(src[c], m)), inv);
+      for (uint32_t c = t; c < a.cols; c += NT)
+        row_store1(a, size_t(row) * a.cols + c, __fmul_rn(expf(__fsub_rn(src[c], m)), inv));
     } else if (OP == kLayerNorm) {
       float s = 0.f;
       for (uint32_t c = t; c < a.cols; c += NT) s += src[c];
@@ -362,7 +392,8 @@ __global__ void __launch_bounds__(512) row_kernel_generic(const RowArgs a) {
       ss = block_reduce<NT>(ss, sf, Add());
       const float inv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(a.cols)), a.eps)));
       for (uint32_t c = t; c < a.cols; c += NT)
-        dst[c] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(src[c], mu), inv), a.gamma[c]), a.beta[c]);
+        row_store1(a, size_t(row) * a.cols + c,
+                   __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(src[c], mu), inv), a.gamma[c]), a.beta[c]));
     } else {
       unsigned long long best = 0ull;
       for (uint32_t c = t; c < a.cols; c += NT) {
@@ -392,6 +423,7 @@ silcu_status run_rows(const char *name, const RowArgs &a, silcu_stream stream) {
   if (a.rows == 0 || a.cols == 0) return SILCU_OK;
   cudaStream_t s = as_stream(stream);
   const bool vec = (a.cols % 4 == 0) && aligned16(a.in) && (!a.out || aligned16(a.out)) &&
+                   (!a.out_lo || aligned16(a.out_lo)) &&
                    (OP != kLayerNorm || (aligned16(a.gamma) && aligned16(a.beta)));
   const uint32_t c = a.cols;
   if (vec && c <= 128) launch_row_warp<OP, 1>(a, s);
@@ -559,7 +591,7 @@ silcu_status silcu_argmax_all_f32(const float *in, size_t n, int64_t *out_index,
 silcu_status silcu_softmax_f32(const float *in, float *out, size_t rows, size_t cols, silcu_stream s) {
   if (rows && cols && (!in || !out)) return fail(SILCU_INVALID_ARGUMENT, "softmax: null pointer");
   if (rows > 0xFFFFFFFFull || cols > 0xFFFFFFFFull) return fail(SILCU_UNSUPPORTED, "softmax: dims >= 2^32");
-  RowArgs a{in, out, nullptr, nullptr, nullptr, uint32_t(rows), uint32_t(cols), 0.f};
+  RowArgs a{in, out, nullptr, nullptr, nullptr, nullptr, uint32_t(rows), uint32_t(cols), 0.f};
   return run_rows<kSoftmax>("softmax", a, s);
 }
 
@@ -568,8 +600,25 @@ silcu_status silcu_layer_norm_f32(const float *in, float *out, const float *gamm
   if (rows && cols && (!in || !out || !gamma || !beta))
     return fail(SILCU_INVALID_ARGUMENT, "layer_norm: null pointer");
   if (rows > 0xFFFFFFFFull || cols > 0xFFFFFFFFull) return fail(SILCU_UNSUPPORTED, "layer_norm: dims >= 2^32");
-  RowArgs a{in, out, nullptr, gamma, beta, uint32_t(rows), uint32_t(cols), eps};
+  RowArgs a{in, out, nullptr, nullptr, gamma, beta, uint32_t(rows), uint32_t(cols), eps};
   return run_rows<kLayerNorm>("layer_norm", a, s);
+}
+
+silcu_status silcu_softmax_split_f32(const float *in, float *out_hi, float *out_lo, size_t rows, size_t cols,
+                                     silcu_stream s) {
+  if (rows && cols && (!in || !out_hi || !out_lo)) return fail(SILCU_INVALID_ARGUMENT, "softmax_split: null pointer");
+  if (rows > 0xFFFFFFFFull || cols > 0xFFFFFFFFull) return fail(SILCU_UNSUPPORTED, "softmax_split: dims >= 2^32");
+  RowArgs a{in, out_hi, out_lo, nullptr, nullptr, nullptr, uint32_t(rows), uint32_t(cols), 0.f};
+  return run_rows<kSoftmax>("softmax_split", a, s);
+}
+
+silcu_status silcu_layer_norm_split_f32(const float *in, float *out_hi, float *out_lo, const float *gamma,
+                                        const float *beta, size_t rows, size_t cols, float eps, silcu_stream s) {
+  if (rows && cols && (!in || !out_hi || !out_lo || !gamma || !beta))
+    return fail(SILCU_INVALID_ARGUMENT, "layer_norm_split: null pointer");
+  if (rows > 0xFFFFFFFFull || cols > 0xFFFFFFFFull) return fail(SILCU_UNSUPPORTED, "layer_norm_split: dims >= 2^32");
+  RowArgs a{in, out_hi, out_lo, nullptr, gamma, beta, uint32_t(rows), uint32_t(cols), eps};
+  return run_rows<kLayerNorm>("layer_norm_split", a, s);
 }
 
 size_t silcu_argmax_workspace_bytes(size_t rows, size_t cols) {
@@ -596,7 +645,7 @@ silcu_status silcu_argmax_f32(const float *in, int32_t *out, size_t rows, size_t
         static_cast<const unsigned long long *>(ws), uint32_t(rows), sp, out);
     return check_launch("argmax(split)", 2);
   }
-  RowArgs a{in, nullptr, out, nullptr, nullptr, uint32_t(rows), uint32_t(cols), 0.f};
+  RowArgs a{in, nullptr, nullptr, out, nullptr, nullptr, uint32_t(rows), uint32_t(cols), 0.f};
   return run_rows<kRowArgmax>("argmax", a, stream);
 }
 

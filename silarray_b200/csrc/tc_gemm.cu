@@ -762,3 +762,16 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
 }
 
 }  // namespace silcu
+
+extern "C" silcu_status silcu_split_f32(const float *src, size_t rows, size_t cols, size_t ld, int transpose,
+                                        float *hi, float *lo, silcu_stream stream) {
+  using namespace silcu;
+  if (rows == 0 || cols == 0) return SILCU_OK;
+  if (!src || !hi || !lo || ld < cols) return fail(SILCU_INVALID_ARGUMENT, "split: bad argument");
+  if (rows > 65535ull * 32 || cols > 65535ull * 32) return fail(SILCU_UNSUPPORTED, "split: extent too large");
+  const int64_t R = transpose ? cols : rows, K = transpose ? rows : cols;
+  const int64_t rs = transpose ? 1 : int64_t(ld), ks = transpose ? int64_t(ld) : 1;
+  dim3 g(uint32_t((K + 31) / 32), uint32_t((R + 31) / 32), 1);
+  pack_split<<<g, 256, 0, as_stream(stream)>>>(src, nullptr, rs, ks, 0, 1, 0, R, K, K, hi, lo);
+  return check_launch("split");
+}

@@ -227,6 +227,36 @@ def layer_norm(IN, OUT=None, gamma=None, beta=None, rows=None, cols=None, eps=1e
     return OUT
 
 
+def softmax_split(IN, rows, cols, OUT_hi=None, OUT_lo=None):
+    """softmax whose result is written as its exact tf32 split (hi, lo)."""
+    _dev(IN, _F32)
+    OUT_hi = torch.empty_like(IN) if OUT_hi is None else _dev(OUT_hi, _F32)
+    OUT_lo = torch.empty_like(IN) if OUT_lo is None else _dev(OUT_lo, _F32)
+    check(lib().silcu_softmax_split_f32(_p(IN), _p(OUT_hi), _p(OUT_lo), rows, cols, _stream()))
+    return OUT_hi, OUT_lo
+
+
+def layer_norm_split(IN, gamma, beta, rows, cols, eps=1e-5, OUT_hi=None, OUT_lo=None):
+    """layer_norm whose result is written as its exact tf32 split (hi, lo)."""
+    _dev(IN, _F32), _dev(gamma, _F32), _dev(beta, _F32)
+    OUT_hi = torch.empty_like(IN) if OUT_hi is None else _dev(OUT_hi, _F32)
+    OUT_lo = torch.empty_like(IN) if OUT_lo is None else _dev(OUT_lo, _F32)
+    check(lib().silcu_layer_norm_split_f32(_p(IN), _p(OUT_hi), _p(OUT_lo), _p(gamma), _p(beta), rows, cols,
+                                           float(eps), _stream()))
+    return OUT_hi, OUT_lo
+
+
+def split(src, rows, cols, ld=None, transpose=False):
+    """Exact tf32 split (hi, lo) of a [rows, cols] matrix, optionally transposed."""
+    _dev(src, _F32)
+    n = rows * cols
+    hi = torch.empty(n, dtype=_F32, device=src.device)
+    lo = torch.empty(n, dtype=_F32, device=src.device)
+    check(lib().silcu_split_f32(_p(src), rows, cols, cols if ld is None else ld, int(transpose), _p(hi), _p(lo),
+                                _stream()))
+    return hi, lo
+
+
 def argmax_f32(IN, OUT=None, rows=None, cols=None):
     _dev(IN, _F32)
     rows, cols = (IN.shape[0], IN.shape[-1]) if rows is None else (rows, cols)

@@ -14,9 +14,9 @@ act, then + residual).  Q, K and V come from one GEMM against [Wq|Wk|Wv]
 (columns are independent, so the values equal three separate GEMMs).
 
 Launches per forward: layer_norm, QKV gemm, scores gemm (batched over
-sequence x head with strided views), softmax, context gemm, Wo gemm
-(+bias +residual), layer_norm, W1 gemm (+bias, relu), W2 gemm (+bias
-+residual).  Every GEMM is the 3xTF32 tcgen05 kernel plus its split pre-pass.
+sequence x head with strided views), softmax, V re-split + context gemm, Wo
+gemm (+bias +residual), layer_norm, W1 gemm (+bias, relu), W2 gemm (+bias
++residual).  Every GEMM is the 3xTF32 tcgen05 kernel.
 """
 from dataclasses import dataclass
 
@@ -85,27 +85,38 @@ def init_input(cfg, seed=1):
 
 
 class Block:
-    """Device-resident weights plus preallocated activations for one config."""
+    """Device-resident weights plus preallocated activations for one config.
+
+    Operands of the tensor-core GEMMs travel as exact tf32 splits (hi, lo):
+    the weights are split (and transposed to K-major) once here; in the
+    forward, layer_norm, softmax and the GEMM epilogues write their results
+    already split, so no GEMM re-reads an operand just to split it (V, read
+    N-major by the context GEMM, is the one operand re-split per forward)."""
 
     def __init__(self, cfg, params, device="cuda"):
         self.cfg = cfg
         self.dev = torch.device(device)
         t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(self.dev)  # noqa: E731
-        d = cfg.d_model
+        d, f = cfg.d_model, cfg.d_ff
         self.g1, self.be1, self.g2, self.be2 = t(params["g1"]), t(params["be1"]), t(params["g2"]), t(params["be2"])
-        self.wqkv = t(np.concatenate([params["wq"], params["wk"], params["wv"]], axis=1))  # [d, 3d]
+        wqkv = t(np.concatenate([params["wq"], params["wk"], params["wv"]], axis=1))  # [d, 3d]
         self.bqkv = t(np.concatenate([params["bq"], params["bk"], params["bv"]]))
-        self.wo, self.bo = t(params["wo"]), t(params["bo"])
-        self.w1, self.b1 = t(params["w1"]), t(params["b1"])
-        self.w2, self.b2 = t(params["w2"]), t(params["b2"])
-        T, f, S, H = cfg.tokens, cfg.d_ff, cfg.seq, cfg.heads
+        self.bo, self.b1, self.b2 = t(params["bo"]), t(params["b1"]), t(params["b2"])
+        # K-major splits of the constant weights: W[K,N] -> (hi, lo) of W^T [N,K]
+        self.wqkv_t = gpu.split(wqkv, d, 3 * d, transpose=True)
+        self.wo_t = gpu.split(t(params["wo"]), d, d, transpose=True)
+        self.w1_t = gpu.split(t(params["w1"]), d, f, transpose=True)
+        self.w2_t = gpu.split(t(params["w2"]), f, d, transpose=True)
+        T, S, H = cfg.tokens, cfg.seq, cfg.heads
         e = lambda *s: torch.empty(*s, dtype=torch.float32, device=self.dev)  # noqa: E731
-        self.h = e(T * d)
-        self.qkv = e(T * 3 * d)
+        pair = lambda n: (e(n), e(n))  # noqa: E731
+        self.h = pair(T * d)
+        self.qkv = pair(T * 3 * d)
         self.scores = e(cfg.batch * H * S * S)
-        self.ctx = e(T * d)
+        self.p = pair(cfg.batch * H * S * S)
+        self.ctx = pair(T * d)
         self.r1 = e(T * d)
-        self.ff = e(T * f)
+        self.ff = pair(T * f)
         self.scale = float(np.float32(1.0) / np.sqrt(np.float32(cfg.head_dim)))
 
     def forward(self, x, out=None):
@@ -113,22 +124,26 @@ class Block:
         T, d, f, S, H, hd, B = cfg.tokens, cfg.d_model, cfg.d_ff, cfg.seq, cfg.heads, cfg.head_dim, cfg.batch
         x = x.reshape(-1)
         out = torch.empty(T * d, dtype=torch.float32, device=self.dev) if out is None else out
-        gpu.layer_norm(x, self.h, self.g1, self.be1, T, d, cfg.eps)
-        gpu.gemm(self.h, self.wqkv, self.qkv, M=T, N=3 * d, K=d, bias=self.bqkv)
+        qh, ql = self.qkv
+        gpu.layer_norm_split(x, self.g1, self.be1, T, d, cfg.eps, *self.h)
+        gpu.gemm(self.h, self.wqkv_t, M=T, N=3 * d, K=d, trans_b=True, bias=self.bqkv,
+                 no_c=True, C_split=self.qkv)
         # scores[b, h] = Q_bh . K_bh^T * scale   (Q_bh rows: qkv[b*S + s, h*hd : h*hd+hd])
-        gpu.gemm(self.qkv, self.qkv[d:], self.scores, M=S, N=S, K=hd, lda=3 * d, ldb=3 * d,
+        gpu.gemm((qh, ql), (qh[d:], ql[d:]), self.scores, M=S, N=S, K=hd, lda=3 * d, ldb=3 * d,
                  trans_b=True, batch=B, stride_a=S * 3 * d, stride_b=S * 3 * d, stride_c=H * S * S,
                  batch_inner=H, stride_a_inner=hd, stride_b_inner=hd, stride_c_inner=S * S,
                  alpha=self.scale)
-        gpu.softmax(self.scores, self.scores, B * H * S, S)
+        gpu.softmax_split(self.scores, B * H * S, S, *self.p)
         # ctx[b*S + s, h*hd + j] = (attn_bh . V_bh)[s, j]
-        gpu.gemm(self.scores, self.qkv[2 * d:], self.ctx, M=S, N=hd, K=S, lda=S, ldb=3 * d, ldc=d,
+        gpu.gemm(self.p, (qh[2 * d:], ql[2 * d:]), M=S, N=hd, K=S, lda=S, ldb=3 * d, ldc=d,
                  batch=B, stride_a=H * S * S, stride_b=S * 3 * d, stride_c=S * d,
-                 batch_inner=H, stride_a_inner=S * S, stride_b_inner=hd, stride_c_inner=hd)
-        gpu.gemm(self.ctx, self.wo, self.r1, M=T, N=d, K=d, bias=self.bo, residual=x)
-        gpu.layer_norm(self.r1, self.h, self.g2, self.be2, T, d, cfg.eps)
-        gpu.gemm(self.h, self.w1, self.ff, M=T, N=f, K=d, bias=self.b1, act="relu")
-        gpu.gemm(self.ff, self.w2, out, M=T, N=d, K=f, bias=self.b2, residual=self.r1)
+                 batch_inner=H, stride_a_inner=S * S, stride_b_inner=hd, stride_c_inner=hd,
+                 no_c=True, C_split=self.ctx)
+        gpu.gemm(self.ctx, self.wo_t, self.r1, M=T, N=d, K=d, trans_b=True, bias=self.bo, residual=x)
+        gpu.layer_norm_split(self.r1, self.g2, self.be2, T, d, cfg.eps, *self.h)
+        gpu.gemm(self.h, self.w1_t, M=T, N=f, K=d, trans_b=True, bias=self.b1, act="relu",
+                 no_c=True, C_split=self.ff)
+        gpu.gemm(self.ff, self.w2_t, out, M=T, N=d, K=f, trans_b=True, bias=self.b2, residual=self.r1)
         return out.reshape(T, d)
 
 
