@@ -1,4 +1,4 @@
-// Test infrastructure only: a stand-in for the subset of Apple Accelerate
+// Linux stand-in for the subset of Apple Accelerate
 // (vDSP, vForce, CBLAS) that the silarray CPU backend calls, so that the
 // reference's own include/cpu.h and include/array.h compile with g++ on Linux.
 //

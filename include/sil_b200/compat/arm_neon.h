@@ -1,4 +1,4 @@
-// Test infrastructure only: scalar stand-in for the four NEON intrinsics the
+// Linux stand-in (scalar) for the four NEON intrinsics the
 // silarray CPU backend uses (include/cpu.h affine).  vfmaq_f32 is a fused
 // multiply-add on ARM, so it maps to fmaf lane by lane.
 #pragma once

@@ -119,7 +119,9 @@ silcu_status silcu_fused_f32(const silcu_program *prog_host, const float *const 
  * Whole-array reductions, single pass over HBM plus a one-block finish.
  * Replace gpu::sum_f32 / min_f32 / max_f32 (include/gpu.h:323-470, which
  * leave <= 256 partials for the host) with an on-device result: `out` is one
- * device scalar.  sum accumulates in fp64 and rounds once.
+ * device scalar.  sum: up to 4096 elements it adds sequentially in fp32 in
+ * index order (bit-identical to the reference's CPU sum); beyond, it
+ * accumulates in fp64 and rounds once.
  * argmax_all writes the first index of the maximum as int64 with the CPU
  * quirk of include/array.h:1733-1740 (values <= FLT_MIN never win; 0 if none). */
 size_t silcu_reduce_workspace_bytes(size_t n);

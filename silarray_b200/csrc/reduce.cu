@@ -187,6 +187,23 @@ __global__ void __launch_bounds__(1024) reduce_finish(const typename RedT<KIND>:
   }
 }
 
+// Small float sums (n <= kSeqSumMax) are added sequentially in fp32, in index
+// order, exactly as the reference's CPU sum (vDSP_sve / std::accumulate,
+// include/cpu.h:266-274) does, so they match it bit for bit; larger sums
+// accumulate in fp64 and round once.
+constexpr int kSeqSumMax = 4096;
+
+__global__ void __launch_bounds__(256) sum_seq_small(const float *__restrict__ in, int n, float *out) {
+  __shared__ float buf[kSeqSumMax];
+  for (int i = threadIdx.x; i < n; i += 256) buf[i] = in[i];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.0f;
+    for (int i = 0; i < n; i++) s = __fadd_rn(s, buf[i]);
+    *out = s;
+  }
+}
+
 int red_grid(uint64_t n) {
   uint64_t want = (n + kRedThreads * 16 - 1) / (kRedThreads * 16);
   uint64_t cap = uint64_t(sm_count()) * kRedCtasPerSm;
@@ -572,6 +589,10 @@ size_t silcu_reduce_workspace_bytes(size_t n) {
 }
 
 silcu_status silcu_sum_f32(const float *in, size_t n, float *out, void *ws, size_t wsb, silcu_stream s) {
+  if (in && out && n > 0 && n <= size_t(kSeqSumMax)) {
+    sum_seq_small<<<1, 256, 0, as_stream(s)>>>(in, int(n), out);
+    return check_launch("sum_f32");
+  }
   return run_reduce<kSum, float, float>("sum_f32", in, n, out, nullptr, ws, wsb, s);
 }
 silcu_status silcu_min_f32(const float *in, size_t n, float *out, void *ws, size_t wsb, silcu_stream s) {
@@ -737,6 +758,10 @@ double *noalloc_partials(silcu_status *st) {
 extern "C" silcu_status silcu_sum_f32_noalloc(const float *in, size_t n, float *out, silcu_stream stream) {
   if (!in || !out) return fail(SILCU_INVALID_ARGUMENT, "sum_f32_noalloc: null pointer");
   if (n == 0) return fail(SILCU_INVALID_ARGUMENT, "sum_f32_noalloc: empty input");
+  if (n <= size_t(kSeqSumMax)) {  // same small-sum rule as silcu_sum_f32; no scratch needed
+    sum_seq_small<<<1, 256, 0, as_stream(stream)>>>(in, int(n), out);
+    return check_launch("sum_f32_noalloc");
+  }
   const int g = red_grid(n);
   if (g > kNoAllocPartials)
     return fail(SILCU_UNSUPPORTED, "sum_f32_noalloc: needs %d partials, the built-in scratch holds %d", g,

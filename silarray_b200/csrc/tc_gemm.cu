@@ -36,9 +36,9 @@ namespace {
 
 constexpr int BM = 128, BK = 32;
 
-// Per-variant constants: BN = 128 (3-stage ring, 4 TMEM chunk buffers, 4
-// epilogue warps) or BN = 256 (2-stage ring, 2 chunk buffers, 8 epilogue
-// warps, each owning 128 columns).  The wider tile halves the shared-memory
+// Per-variant constants: BN = 64 (4-stage ring, 8 TMEM chunk buffers, 4
+// epilogue warps of 64 columns), BN = 128 (3 stages, 4 buffers, 4 warps) or
+// BN = 256 (2 stages, 2 buffers, 8 epilogue warps of 128 columns).  The wider tile halves the shared-memory
 // operand traffic per FLOP of A, which bounds the 128-wide variant.
 template <int BN_>
 struct Cfg {
@@ -48,7 +48,8 @@ struct Cfg {
   static constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_B;  // Ahi, Alo, Bhi, Blo
   static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
-  static constexpr int EPI_WARPS = BN / 32;
+  static constexpr int EC = BN >= 128 ? 128 : BN;  // columns per epilogue warp
+  static constexpr int EPI_WARPS = 4 * (BN / EC);
   static constexpr int OUT_STAGE_BYTES = EPI_WARPS * 4096;  // one 32x32 fp32 block per epilogue warp
   static constexpr int SMEM_BYTES = RING_BYTES + OUT_STAGE_BYTES + 1024 + 256;
   static constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
@@ -372,7 +373,7 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
     bool ok = true;
     for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
       const Tile tl = decode_tile<BN>(p, tile);
-      constexpr int EC = 128;  // columns per epilogue warp
+      constexpr int EC = C::EC;
       float acc[EC];
 #pragma unroll
       for (int i = 0; i < EC; i++) acc[i] = 0.0f;
@@ -651,7 +652,7 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
     return fail(SILCU_WORKSPACE_TOO_SMALL, "sgemm(tc): workspace %zu < %zu", wsb, need);
   if (a.M > (1 << 30) || a.N > (1 << 30) || Kp > (1 << 30))
     return fail(SILCU_UNSUPPORTED, "sgemm(tc): extent >= 2^30");
-  const int BN = a.N > 128 ? 256 : 128;  // wide tiles unless N is small
+  const int BN = a.N > 128 ? 256 : (a.N > 64 ? 128 : 64);  // wide tiles unless N is small
   const int64_t tiles_m = (a.M + BM - 1) / BM, tiles_n = (a.N + BN - 1) / BN;
   const int64_t nb = total_batch(a), bin = a.batch_inner > 1 ? a.batch_inner : 1, bout = a.batch;
   if (tiles_m * tiles_n * nb > 0x7FFFFFFF) return fail(SILCU_UNSUPPORTED, "sgemm(tc): too many tiles");
@@ -758,7 +759,9 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
   if (!p.err) return fail(SILCU_CUDA_ERROR, "sgemm(tc): no device error word");
   const int64_t total = tiles_m * tiles_n * nb;
   const uint32_t grid = uint32_t(total < sm_count() ? total : sm_count());
-  return BN == 256 ? launch_tc<256>(p, grid, s) : launch_tc<128>(p, grid, s);
+  if (BN == 256) return launch_tc<256>(p, grid, s);
+  if (BN == 128) return launch_tc<128>(p, grid, s);
+  return launch_tc<64>(p, grid, s);
 }
 
 }  // namespace silcu

@@ -133,3 +133,10 @@ def test_layer_norm_known_answer(cuda):
 def test_softmax_known_answer(cuda):
     x = np.array([[1, 2, 3]], np.float32)
     np.testing.assert_allclose(host(gpu.softmax(dev(x))), [[0.0900, 0.2447, 0.6652]], atol=1e-3)
+
+
+@pytest.mark.parametrize("n", [1, 6, 1000, 4096])
+def test_small_sum_is_sequential_fp32(cuda, n):
+    """Up to 4096 elements the sum is the reference's sequential fp32 sum, bit for bit."""
+    x = np.random.default_rng(n).uniform(-1, 1, n).astype(np.float32)
+    assert host(gpu.sum_f32(dev(x))) == O.sum_all(x)
