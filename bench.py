@@ -308,7 +308,10 @@ def run_ours(args):
         traffic_path = os.path.join(ROOT, "profiles", "traffic.json")
         traffic = None
         if os.path.exists(traffic_path):
+            # captured at the full single-GPU shape (M = 16384); scaled by rows otherwise
             traffic = json.load(open(traffic_path)).get("tc_gemm_kernel_ffn_up")
+            if traffic is not None and T != 16384:
+                traffic = traffic * T / 16384.0
         roofline = {"bound": "tensor", "kernel": "tc_gemm_kernel<256> M=%d N=%d K=%d (FFN-up of the forward)" % (T, f, d),
                     "achieved": achieved, "peak": ceiling, "unit": "TFLOP/s", "frac": achieved / ceiling,
                     "traffic": traffic,
