@@ -38,6 +38,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sgemm", action="store_true", help="skip the 8192^3 SGEMM side measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--suite", action="store_true",
+                    help="measure every configuration of the metric (one JSON line each) instead of the headline")
     ap.add_argument("--profile-case", default=None, choices=["gemm", "block"],
                     help="run only a small case for ncu: the FFN-up GEMM of the workload, or a 2-sequence block")
     return ap.parse_args()
@@ -77,6 +79,147 @@ def profile_case(args):
     torch.cuda.synchronize()
     gpu.device_status()
     print("profile case done", flush=True)
+    return 0
+
+
+def run_suite(args):
+    """Every configuration of BASELINE.json's metric on one GPU: algorithmic
+    bytes or FLOPs per call / CUDA-event time (L2 flushed before each timed
+    call), against the measured HBM copy bandwidth or the 3xTF32 ceiling."""
+    import numpy as np
+    import torch
+    from silarray_b200 import gpu
+    dev = torch.device("cuda", 0)
+    hbm, bf16, src = peaks()
+    ceiling = bf16 / 6.0
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def timed(fn, iters=max(3, args.steps)):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(iters):
+            flush.zero_()
+            s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            fn()
+            e0.record()
+            torch.cuda.synchronize()
+            ts.append(s0.elapsed_time(e0))
+        return float(np.median(ts)) / 1e3
+
+    def timed_graph(make_fn, set_bytes, reps=20):
+        """Short kernels: `reps` calls captured in one CUDA graph, each on its
+        own input set (make_fn(i) returns the call), so that the sets in
+        rotation exceed twice the L2 and host launch latency is not timed."""
+        nsets = max(2, int(np.ceil(2 * 126e6 / max(1, set_bytes))))
+        calls = [make_fn(i % nsets) for i in range(reps)]
+        for c in calls[:nsets]:
+            c()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            with torch.cuda.graph(gr, stream=st):
+                for c in calls:
+                    c()
+        torch.cuda.current_stream().wait_stream(st)
+        gr.replay()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(max(3, args.steps)):
+            flush.zero_()
+            s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            gr.replay()
+            e0.record()
+            torch.cuda.synchronize()
+            ts.append(s0.elapsed_time(e0))
+        return float(np.median(ts)) / 1e3 / reps
+
+    def emit(name, sec, nbytes=None, flops=None, **extra):
+        line = {"config": name, "ms": sec * 1e3}
+        if nbytes is not None:
+            line.update({"GB/s": nbytes / sec / 1e9, "frac_of_hbm": nbytes / sec / 1e9 / hbm, "bytes": nbytes})
+        if flops is not None:
+            line.update({"TFLOP/s": flops / sec / 1e12, "frac_of_3xtf32_ceiling": flops / sec / 1e12 / ceiling})
+        line.update(extra)
+        print(json.dumps(line), flush=True)
+
+    U = lambda *sh: torch.rand(*sh, device=dev, generator=g) * 2 - 1  # noqa: E731
+    Nn = lambda std, *sh: torch.randn(*sh, device=dev, generator=g) * std  # noqa: E731
+    for n in (1024, 8192):
+        a, b, c = U(n, n), U(n, n), torch.empty(n * n, device=dev)
+        emit(f"sgemm {n}^3", timed(lambda: gpu.gemm(a, b, c, M=n, N=n, K=n)), flops=2.0 * n ** 3)
+        del a, b, c
+    gv_bytes = 4.0 * (4096 * 4096 + 4096 + 2 * 4096)
+    gsets = {}
+
+    def gemv_set(i):
+        if i not in gsets:
+            gsets[i] = (Nn(1, 4096), Nn(0.02, 4096, 4096), Nn(0.01, 4096), torch.empty(4096, device=dev))
+        x, W, bb, y = gsets[i]
+        return lambda: gpu.sgemv(x, W, y, 4096, 4096, bias=bb)
+    emit("gemv 1x4096 . 4096x4096 + b", timed_graph(gemv_set, gv_bytes), nbytes=gv_bytes, timing="graph")
+    gsets.clear()
+    sb_bytes = 4.0 * (32 * 4096 + 4096 * 768 + 32 * 768)
+
+    def sb_set(i):
+        if i not in gsets:
+            gsets[i] = (Nn(1, 32, 4096), Nn(0.02, 4096, 768), torch.empty(32 * 768, device=dev))
+        X, W2, Y = gsets[i]
+        return lambda: gpu.gemm(X, W2, Y, M=32, N=768, K=4096)
+    emit("small batch 32x4096 . 4096x768", timed_graph(sb_set, sb_bytes), nbytes=sb_bytes,
+         flops=2.0 * 32 * 4096 * 768, timing="graph")
+    gsets.clear()
+    for C in (1024, 8192, 32768):
+        R = 4096
+        gm, bt = 1 + Nn(0.1, C), Nn(0.1, C)
+        if C < 32768:  # < 2 x L2 per call: graph replays over rotating inputs
+            sets = {}
+
+            def rows_set(i):
+                if i not in sets:
+                    sets[i] = (Nn(2, R, C), torch.empty(R, C, device=dev), torch.empty(R, dtype=torch.int32,
+                                                                                      device=dev))
+                return sets[i]
+            for name, nb, mk in (
+                    ("softmax", 8.0 * R * C, lambda i: (lambda X=rows_set(i): gpu.softmax(X[0], X[1]))),
+                    ("layer_norm", 8.0 * R * C + 8.0 * C,
+                     lambda i: (lambda X=rows_set(i): gpu.layer_norm(X[0], X[1], gm, bt))),
+                    ("argmax(axis=1)", 4.0 * R * C + 4.0 * R,
+                     lambda i: (lambda X=rows_set(i): gpu.argmax_f32(X[0], X[2]))),
+                    ("sum(axis=1)", 4.0 * R * C + 4.0 * R,
+                     lambda i: (lambda X=rows_set(i): gpu.sum_axis_f32(X[0], R, C, 1, X[1].view(-1)[:R])))):
+                emit(f"{name} 4096x{C}", timed_graph(mk, nb), nbytes=nb, timing="graph")
+            sets.clear()
+            continue
+        X = Nn(2, R, C)
+        Y = torch.empty_like(X)
+        emit(f"softmax 4096x{C}", timed(lambda: gpu.softmax(X, Y)), nbytes=8.0 * R * C)
+        emit(f"layer_norm 4096x{C}", timed(lambda: gpu.layer_norm(X, Y, gm, bt)), nbytes=8.0 * R * C + 8.0 * C)
+        emit(f"argmax(axis=1) 4096x{C}", timed(lambda: gpu.argmax_f32(X)), nbytes=4.0 * R * C + 4.0 * R)
+        emit(f"sum(axis=1) 4096x{C}", timed(lambda: gpu.sum_axis_f32(X, R, C, 1)), nbytes=4.0 * R * C + 4.0 * R)
+        del X, Y
+    Z = U(1 << 28)
+    for name, fn in (("sum", gpu.sum_f32), ("min", gpu.min_f32), ("max", gpu.max_f32),
+                     ("argmax", gpu.argmax_all_f32)):
+        emit(f"global {name} 2^28", timed(lambda: fn(Z)), nbytes=4.0 * (1 << 28))
+    del Z
+    BH, S, d = 128, 1024, 64
+    Q, Kt, V = Nn(1, BH, S, d), Nn(1, BH, d, S), Nn(1, BH, S, d)
+    Sc, O = torch.empty(BH * S * S, device=dev), torch.empty(BH * S * d, device=dev)
+
+    def attention():
+        gpu.gemm(Q, Kt, Sc, M=S, N=S, K=d, batch=BH, stride_a=S * d, stride_b=d * S, stride_c=S * S,
+                 alpha=0.125)
+        gpu.softmax(Sc, Sc, BH * S, S)
+        gpu.gemm(Sc, V, O, M=S, N=d, K=S, batch=BH, stride_a=S * S, stride_b=S * d, stride_c=S * d)
+    emit("bmm attention 128x1024x1024x64", timed(attention), flops=4.0 * BH * S * S * d,
+         hbm_bytes_unfused=4.0 * BH * S * S * 4)
     return 0
 
 
@@ -363,6 +506,8 @@ def main():
         args.warmup = 3
     if args.profile_case:
         return profile_case(args)
+    if args.suite:
+        return run_suite(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
