@@ -231,7 +231,7 @@ silcu_status run_reduce(const char *name, const In *in, size_t n, Out *out, floa
 }
 
 // ------------------------------------------------------------------ row ops
-enum RowOp { kSoftmax = 0, kLayerNorm = 1, kRowArgmax = 2 };
+enum RowOp { kSoftmax = 0, kLayerNorm = 1, kRowArgmax = 2, kRowSum = 3 };
 
 struct RowArgs {
   const float *in;
@@ -354,21 +354,29 @@ __global__ void __launch_bounds__(WARP ? 256 : NT) row_kernel(const RowArgs a) {
           row_store4(a, row, c, o);
         }
       }
-    } else {  // argmax
-      unsigned long long best = 0ull;
+    } else if (OP == kRowSum) {
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < VPT; j++) sum += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+      sum = row_reduce<NT, WARP>(sum, sf, Add());
+      if (t == 0) a.out[row] = sum;
+    } else {  // argmax: each thread scans its elements in increasing index
+      // order with the reference's rule (running max starts at FLT_MIN,
+      // strict '>'), then one 64-bit key per thread settles value and index.
+      float bv = FLT_MIN;
+      int32_t bi = -1;
 #pragma unroll
       for (int j = 0; j < VPT; j++) {
         const uint32_t c = t + j * NT;
         if (c < c4) {
-          const uint32_t base = c * 4;
-          unsigned long long k0 = amax_key(v[j].x, base), k1 = amax_key(v[j].y, base + 1);
-          unsigned long long k2 = amax_key(v[j].z, base + 2), k3 = amax_key(v[j].w, base + 3);
-          k0 = k0 > k1 ? k0 : k1;
-          k2 = k2 > k3 ? k2 : k3;
-          k0 = k0 > k2 ? k0 : k2;
-          best = best > k0 ? best : k0;
+          const int32_t base = int32_t(c * 4);
+          if (v[j].x > bv) { bv = v[j].x; bi = base; }
+          if (v[j].y > bv) { bv = v[j].y; bi = base + 1; }
+          if (v[j].z > bv) { bv = v[j].z; bi = base + 2; }
+          if (v[j].w > bv) { bv = v[j].w; bi = base + 3; }
         }
       }
+      unsigned long long best = bi >= 0 ? amax_key(bv, uint32_t(bi)) : 0ull;
       best = row_reduce<NT, WARP>(best, sk, Max());
       if (t == 0) a.idx[row] = best ? int32_t(0xFFFFFFFFu - uint32_t(best & 0xFFFFFFFFu)) : 0;
     }
@@ -439,7 +447,7 @@ template <int OP>
 silcu_status run_rows(const char *name, const RowArgs &a, silcu_stream stream) {
   if (a.rows == 0 || a.cols == 0) return SILCU_OK;
   cudaStream_t s = as_stream(stream);
-  const bool vec = (a.cols % 4 == 0) && aligned16(a.in) && (!a.out || aligned16(a.out)) &&
+  const bool vec = (a.cols % 4 == 0) && aligned16(a.in) && (!a.out || aligned16(a.out) || OP == kRowSum) &&
                    (!a.out_lo || aligned16(a.out_lo)) &&
                    (OP != kLayerNorm || (aligned16(a.gamma) && aligned16(a.beta)));
   const uint32_t c = a.cols;
@@ -685,6 +693,10 @@ silcu_status silcu_sum_axis_f32(const float *in, float *out, size_t outer, size_
   if (len == 0) {
     cudaError_t e = cudaMemsetAsync(out, 0, total * sizeof(float), s);
     return e == cudaSuccess ? SILCU_OK : fail(SILCU_CUDA_ERROR, "sum_axis: %s", cudaGetErrorString(e));
+  }
+  if (inner == 1 && len % 4 == 0 && len <= 32768 && outer <= 0xFFFFFFFFull && aligned16(in)) {
+    RowArgs a{in, out, nullptr, nullptr, nullptr, nullptr, uint32_t(outer), uint32_t(len), 0.f};
+    return run_rows<kRowSum>("sum_axis(rows)", a, stream);
   }
   if (inner == 1) {
     if (len <= 256) {
