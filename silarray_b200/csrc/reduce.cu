@@ -9,6 +9,7 @@
 // Row ops keep the whole row on chip: each thread holds VPT float4 of the
 // row in registers, so softmax and layer_norm read HBM once and write once
 // (the reference reads the row 2-3 times: include/gpu_kernels.metal:1316-1467).
+#include <cooperative_groups.h>
 #include <float.h>
 
 #include "common.cuh"
@@ -383,6 +384,145 @@ __global__ void __launch_bounds__(WARP ? 256 : NT) row_kernel(const RowArgs a) {
   }
 }
 
+// Long rows: a cluster of 4 CTAs shares one row (each holds a quarter in
+// registers); partial maxima / sums / argmax keys meet through distributed
+// shared memory, summed in cluster-rank order on every CTA (deterministic).
+// With 256-thread CTAs several rows are in flight per SM, which a single
+// 1024-thread CTA per row cannot do.  Requires cols % 16 == 0.
+constexpr int kClusterCtas = 4;
+
+template <int OP, int VPT>
+__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256)
+    row_cluster_kernel(const RowArgs a) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  constexpr int NT = 256;
+  __shared__ float sf[NT / 32];
+  __shared__ unsigned long long sk[NT / 32];
+  __shared__ float xf[2];
+  __shared__ unsigned long long xk;
+  const int t = threadIdx.x;
+  const uint32_t rank = cl.block_rank();
+  const uint32_t row = blockIdx.x / kClusterCtas;
+  const uint32_t part = a.cols / 4 / kClusterCtas;  // float4 per CTA
+  const uint32_t c0 = rank * part;
+  const float4 *src = reinterpret_cast<const float4 *>(a.in + size_t(row) * a.cols);
+  float4 v[VPT];
+#pragma unroll
+  for (int j = 0; j < VPT; j++) {
+    const uint32_t c = t + j * NT;
+    v[j] = c < part ? __ldcs(src + c0 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  auto cl_sum = [&](float x, int slot) {
+    x = block_reduce<NT>(x, sf, Add());
+    if (t == 0) xf[slot] = x;
+    cl.sync();
+    float r = 0.f;
+#pragma unroll
+    for (int q = 0; q < kClusterCtas; q++) r += *cl.map_shared_rank(&xf[slot], q);
+    return r;
+  };
+  if (OP == kSoftmax) {
+    float m = __int_as_float(0xff800000);
+#pragma unroll
+    for (int j = 0; j < VPT; j++)
+      if (t + j * NT < part) m = fmaxf(m, fmaxf(fmaxf(v[j].x, v[j].y), fmaxf(v[j].z, v[j].w)));
+    m = block_reduce<NT>(m, sf, Max());
+    if (t == 0) xf[0] = m;
+    cl.sync();
+#pragma unroll
+    for (int q = 0; q < kClusterCtas; q++) m = fmaxf(m, *cl.map_shared_rank(&xf[0], q));
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; j++) {
+      if (t + j * NT < part) {
+        v[j].x = expf(__fsub_rn(v[j].x, m));
+        v[j].y = expf(__fsub_rn(v[j].y, m));
+        v[j].z = expf(__fsub_rn(v[j].z, m));
+        v[j].w = expf(__fsub_rn(v[j].w, m));
+        s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+      }
+    }
+    s = cl_sum(s, 1);
+    const float inv = __frcp_rn(s);
+#pragma unroll
+    for (int j = 0; j < VPT; j++) {
+      const uint32_t c = t + j * NT;
+      if (c < part)
+        row_store4(a, row, c0 + c, make_float4(__fmul_rn(v[j].x, inv), __fmul_rn(v[j].y, inv),
+                                               __fmul_rn(v[j].z, inv), __fmul_rn(v[j].w, inv)));
+    }
+  } else if (OP == kLayerNorm) {
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; j++) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+    s = cl_sum(s, 0);
+    const float mu = __fdiv_rn(s, float(a.cols));
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; j++) {
+      if (t + j * NT < part) {
+        v[j].x = __fsub_rn(v[j].x, mu);
+        v[j].y = __fsub_rn(v[j].y, mu);
+        v[j].z = __fsub_rn(v[j].z, mu);
+        v[j].w = __fsub_rn(v[j].w, mu);
+        ss += (__fmul_rn(v[j].x, v[j].x) + __fmul_rn(v[j].y, v[j].y)) +
+              (__fmul_rn(v[j].z, v[j].z) + __fmul_rn(v[j].w, v[j].w));
+      }
+    }
+    ss = cl_sum(ss, 1);
+    const float inv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(a.cols)), a.eps)));
+    const float4 *g4 = reinterpret_cast<const float4 *>(a.gamma);
+    const float4 *b4 = reinterpret_cast<const float4 *>(a.beta);
+#pragma unroll
+    for (int j = 0; j < VPT; j++) {
+      const uint32_t c = t + j * NT;
+      if (c < part) {
+        const float4 g = __ldg(g4 + c0 + c), b = __ldg(b4 + c0 + c);
+        float4 o;
+        o.x = __fadd_rn(__fmul_rn(__fmul_rn(v[j].x, inv), g.x), b.x);
+        o.y = __fadd_rn(__fmul_rn(__fmul_rn(v[j].y, inv), g.y), b.y);
+        o.z = __fadd_rn(__fmul_rn(__fmul_rn(v[j].z, inv), g.z), b.z);
+        o.w = __fadd_rn(__fmul_rn(__fmul_rn(v[j].w, inv), g.w), b.w);
+        row_store4(a, row, c0 + c, o);
+      }
+    }
+  } else if (OP == kRowSum) {
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; j++) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+    s = cl_sum(s, 0);
+    if (rank == 0 && t == 0) a.out[row] = s;
+  } else {
+    float bv = FLT_MIN;
+    int32_t bi = -1;
+#pragma unroll
+    for (int j = 0; j < VPT; j++) {
+      const uint32_t c = t + j * NT;
+      if (c < part) {
+        const int32_t base = int32_t((c0 + c) * 4);
+        if (v[j].x > bv) { bv = v[j].x; bi = base; }
+        if (v[j].y > bv) { bv = v[j].y; bi = base + 1; }
+        if (v[j].z > bv) { bv = v[j].z; bi = base + 2; }
+        if (v[j].w > bv) { bv = v[j].w; bi = base + 3; }
+      }
+    }
+    unsigned long long best = bi >= 0 ? amax_key(bv, uint32_t(bi)) : 0ull;
+    best = block_reduce<NT>(best, sk, Max());
+    if (t == 0) xk = best;
+    cl.sync();
+    if (rank == 0 && t == 0) {
+#pragma unroll
+      for (int q = 0; q < kClusterCtas; q++) {
+        const unsigned long long k = *cl.map_shared_rank(&xk, q);
+        best = best > k ? best : k;
+      }
+      a.idx[row] = best ? int32_t(0xFFFFFFFFu - uint32_t(best & 0xFFFFFFFFu)) : 0;
+    }
+  }
+  cl.sync();  // peers may still be reading this CTA's exchange slots
+}
+
 // Generic fallback: any cols (no alignment requirement), re-reads the row
 // from global memory (the second read hits L2 for rows up to a few MB).
 template <int OP>
@@ -458,6 +598,10 @@ silcu_status run_rows(const char *name, const RowArgs &a, silcu_stream stream) {
   else if (vec && c <= 2048) launch_row<OP, 256, 2>(a, s);
   else if (vec && c <= 4096) launch_row<OP, 256, 4>(a, s);
   else if (vec && c <= 8192) launch_row<OP, 512, 4>(a, s);
+  else if (vec && c <= 16384 && (c % 16 == 0) && a.rows <= 0x3FFFFFFFu)
+    row_cluster_kernel<OP, 4><<<a.rows * kClusterCtas, 256, 0, s>>>(a);
+  else if (vec && c <= 32768 && (c % 16 == 0) && a.rows <= 0x3FFFFFFFu)
+    row_cluster_kernel<OP, 8><<<a.rows * kClusterCtas, 256, 0, s>>>(a);
   else if (vec && c <= 16384) launch_row<OP, 512, 8>(a, s);
   else if (vec && c <= 32768) launch_row<OP, 1024, 8>(a, s);
   else row_kernel_generic<OP><<<a.rows < 65535u * 16 ? a.rows : 65535u * 16, 512, 0, s>>>(a);
