@@ -40,7 +40,7 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--suite", action="store_true",
                     help="measure every configuration of the metric (one JSON line each) instead of the headline")
-    ap.add_argument("--profile-case", default=None, choices=["gemm", "block"],
+    ap.add_argument("--profile-case", default=None, choices=["gemm", "block", "attention"],
                     help="run only a small case for ncu: the FFN-up GEMM of the workload, or a 2-sequence block")
     return ap.parse_args()
 
@@ -70,6 +70,16 @@ def profile_case(args):
         gargs = ffn_up_case(dev)
         for _ in range(args.warmup + 1):
             gpu.gemm(**gargs)
+    elif args.profile_case == "attention":
+        BH, S, d = 32, 1024, 64  # the BMM-attention config at a quarter of its batch
+        g = torch.Generator(device=dev).manual_seed(0)
+        qs = gpu.split(torch.randn(BH * S * d, device=dev, generator=g), BH * S, d)
+        ks = gpu.split(torch.randn(BH * S * d, device=dev, generator=g), BH * S, d)
+        vt = gpu.transpose_split(torch.randn(BH * S * d, device=dev, generator=g), S, d, d, batch=BH, s_b=S * d)
+        Ob = torch.empty(BH * S * d, device=dev)
+        for _ in range(args.warmup + 1):
+            gpu.attention(qs, ks, vt, Sq=S, Sk=S, batch=BH, heads=1, ldq=d, sq_b=S * d, sq_h=S * d, ldk=d,
+                          sk_b=S * d, sk_h=S * d, ldv=S, sv_b=d * S, sv_h=d * S, scale=0.125, O=Ob)
     else:
         cfg = transformer.Config(batch=2)
         blk = transformer.Block(cfg, transformer.init_params(cfg), device=dev)
@@ -211,15 +221,17 @@ def run_suite(args):
     del Z
     BH, S, d = 128, 1024, 64
     Q, Kt, V = Nn(1, BH, S, d), Nn(1, BH, d, S), Nn(1, BH, S, d)
-    Sc, O = torch.empty(BH * S * S, device=dev), torch.empty(BH * S * d, device=dev)
+    Ob = torch.empty(BH * S * d, device=dev)
 
     def attention():
-        gpu.gemm(Q, Kt, Sc, M=S, N=S, K=d, batch=BH, stride_a=S * d, stride_b=d * S, stride_c=S * S,
-                 alpha=0.125)
-        gpu.softmax(Sc, Sc, BH * S, S)
-        gpu.gemm(Sc, V, O, M=S, N=d, K=S, batch=BH, stride_a=S * S, stride_b=S * d, stride_c=S * d)
-    emit("bmm attention 128x1024x1024x64", timed(attention), flops=4.0 * BH * S * S * d,
-         hbm_bytes_unfused=4.0 * BH * S * S * 4)
+        # operands to their split K-major forms (K from the stored K^T, V^T from V), then one fused kernel
+        qs = gpu.split(Q, BH * S, d)
+        ks = gpu.transpose_split(Kt, d, S, S, batch=BH, s_b=d * S)
+        vt = gpu.transpose_split(V, S, d, d, batch=BH, s_b=S * d)
+        gpu.attention(qs, ks, vt, Sq=S, Sk=S, batch=BH, heads=1, ldq=d, sq_b=S * d, sq_h=S * d,
+                      ldk=d, sk_b=S * d, sk_h=S * d, ldv=S, sv_b=d * S, sv_h=d * S, scale=0.125, O=Ob)
+    emit("bmm attention 128x1024x1024x64 (fused)", timed(attention), flops=4.0 * BH * S * S * d,
+         note="includes the splits of Q, K^T->K and V->V^T")
     return 0
 
 

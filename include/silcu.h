@@ -225,6 +225,38 @@ typedef struct silcu_gemm_args {
 silcu_status silcu_split_f32(const float *src, size_t rows, size_t cols, size_t ld, int transpose, float *hi,
                              float *lo, silcu_stream stream);
 
+/* Batched transposing split: block (b, h) of the source, a [rows, cols]
+ * matrix at src + b*s_b + h*s_h with row stride ld, becomes the contiguous
+ * [cols, rows] block b*heads + h of hi/lo.  When src_lo is given the source is
+ * itself a split pair (value = src + src_lo, exact).  Used to turn V [S, D]
+ * into the K-major V^T operand of silcu_attention_f32.  No reference counterpart. */
+silcu_status silcu_transpose_split_f32(const float *src, const float *src_lo, size_t rows, size_t cols, size_t ld,
+                                       size_t batch, size_t heads, size_t s_b, size_t s_h, float *hi, float *lo,
+                                       silcu_stream stream);
+
+/* ------------------------------------------------------------ attention
+ * O = softmax(fl(Q . K^T * scale)) . V per (batch, head), fused in one
+ * kernel: the score matrix never reaches HBM.  The reference computes this
+ * chain node by node (Q.dot(K.transpose()) * scale, softmax, .dot(V):
+ * gpu::dot_f32_ex, gpu::affine, gpu::softmax, gpu::sgemm_steel of
+ * include/gpu.h:1296-1328, 985-1004, 916-942, 577-581); both products here
+ * are 3xTF32 and the softmax is the streaming form over key blocks, equal to
+ * the node-by-node result within fp32 rounding.  Operands are exact tf32
+ * splits (hi/lo): Q [Sq, D] rows, K [Sk, D] rows, V^T [D, Sk] rows, each at
+ * X + b*s_b + h*s_h with its row stride.  D = 64.  Outputs: O [Sq, D] fp32
+ * and/or its split.  16-byte aligned rows and strides. */
+typedef struct silcu_attention_args {
+  const float *Q_hi, *Q_lo, *K_hi, *K_lo, *Vt_hi, *Vt_lo;
+  float *O, *O_hi, *O_lo;
+  int64_t Sq, Sk, D, batch, heads;
+  int64_t ldq, sq_b, sq_h;
+  int64_t ldk, sk_b, sk_h;
+  int64_t ldv, sv_b, sv_h;
+  int64_t ldo, so_b, so_h;
+  float scale;
+} silcu_attention_args;
+silcu_status silcu_attention_f32(const silcu_attention_args *args_host, silcu_stream stream);
+
 size_t silcu_sgemm_workspace_bytes(const silcu_gemm_args *args_host);
 silcu_status silcu_sgemm_ex(const silcu_gemm_args *args_host, void *workspace, size_t workspace_bytes,
                             silcu_stream stream);

@@ -53,6 +53,17 @@ class GemmArgs(C.Structure):
                 ("A_hi", vp), ("A_lo", vp), ("B_hi", vp), ("B_lo", vp), ("C_hi", vp), ("C_lo", vp)]
 
 
+class AttnArgs(C.Structure):
+    _fields_ = [("Q_hi", vp), ("Q_lo", vp), ("K_hi", vp), ("K_lo", vp), ("Vt_hi", vp), ("Vt_lo", vp),
+                ("O", vp), ("O_hi", vp), ("O_lo", vp),
+                ("Sq", i64), ("Sk", i64), ("D", i64), ("batch", i64), ("heads", i64),
+                ("ldq", i64), ("sq_b", i64), ("sq_h", i64),
+                ("ldk", i64), ("sk_b", i64), ("sk_h", i64),
+                ("ldv", i64), ("sv_b", i64), ("sv_h", i64),
+                ("ldo", i64), ("so_b", i64), ("so_h", i64),
+                ("scale", f32)]
+
+
 _SIGS = {
     "silcu_last_error": ([], C.c_char_p),
     "silcu_abi_version": ([], C.c_int),
@@ -78,6 +89,8 @@ _SIGS = {
     "silcu_softmax_split_f32": ([vp, vp, vp, sz, sz, vp], C.c_int),
     "silcu_layer_norm_split_f32": ([vp, vp, vp, vp, vp, sz, sz, f32, vp], C.c_int),
     "silcu_split_f32": ([vp, sz, sz, sz, C.c_int, vp, vp, vp], C.c_int),
+    "silcu_transpose_split_f32": ([vp, vp, sz, sz, sz, sz, sz, sz, sz, vp, vp, vp], C.c_int),
+    "silcu_attention_f32": ([C.POINTER(AttnArgs), vp], C.c_int),
     "silcu_argmax_workspace_bytes": ([sz, sz], sz),
     "silcu_sum_axis_workspace_bytes": ([sz, sz, sz], sz),
     "silcu_sum_axis_f32": ([vp, vp, sz, sz, sz, vp, sz, vp], C.c_int),

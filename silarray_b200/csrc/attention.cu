@@ -1,0 +1,409 @@
+// Fused attention on the 5th-generation tensor cores: O = softmax(Q.K^T * scale) . V
+// per (batch, head), without writing the score matrix to HBM.
+//
+// This fuses the reference's attention chain (bench/composite/bench_transformer.cpp:
+// Q.dot(K.transpose()) * scale -> softmax -> .dot(V), i.e. gpu::dot_f32_ex,
+// gpu::affine, gpu::softmax and gpu::sgemm_steel of include/gpu.h) into one
+// kernel.  Both products are 3xTF32 (x = hi + lo, hi*hi + hi*lo + lo*hi) on
+// tcgen05.mma; each score is rounded once as fl(dot * scale) as the reference's
+// affine node does; the softmax is the streaming (online) form over key blocks
+// of 64, so the result equals the reference's up to fp32 rounding.
+//
+// One CTA = 128 query rows of one (batch, head); D = 64.
+//   warp 0     TMA: Q once (hi/lo), K blocks in a 2-stage ring, V^T blocks
+//   warp 1     TMEM alloc; one thread issues S_j = Q K_j^T into a double
+//              buffer, then O_j = P_{j-1} V_{j-1}, so S_{j+1} overlaps the
+//              softmax of block j
+//   warps 2-9  thread = query row (two warps per row quarter, each with half
+//              of the keys and of the output columns): scores from TMEM, running max / sum,
+//              P_j split into hi/lo into TMEM (the A operand of the P.V
+//              MMA), O accumulated in registers with
+//              round-to-nearest adds and rescaled as the max moves.
+// Shared memory: Q 64 KB + K 2 x 32 KB + V^T 2 x 32 KB = 192 KB.  P lives in
+// TMEM (the A operand of P.V is read from tensor memory), double-buffered
+// with O and the scores, so the softmax of block j + 1 overlaps P.V of block j.
+// All waits are bounded (as in tc_gemm.cu); no TMA multicast, no clusters.
+#include <stdlib.h>
+#include <string.h>
+
+#include "common.cuh"
+#include "tc_common.cuh"
+
+namespace silcu {
+namespace {
+using namespace tc;
+
+constexpr int QT = 128;  // query rows per CTA
+constexpr int KB = 64;   // keys per block
+constexpr int HD = 64;   // head dimension
+constexpr int Q_ATOM = QT * 128;           // 16 KB: 128 rows x 32 fp32
+constexpr int K_ATOM = KB * 128;           // 8 KB
+constexpr int Q_BYTES = 2 * 2 * Q_ATOM;    // hi, lo x 2 atoms = 64 KB
+constexpr int K_STAGE = 2 * 2 * K_ATOM;    // 32 KB
+constexpr int V_BYTES = 2 * 2 * K_ATOM;    // V^T: 64 hd rows x 64 keys, hi/lo = 32 KB
+constexpr int OFF_Q = 0, OFF_K = Q_BYTES, OFF_V = OFF_K + 2 * K_STAGE;
+constexpr int DATA_BYTES = OFF_V + 2 * V_BYTES;  // 192 KB of 1024-aligned operand buffers
+// Ahead of them: 14 mbarriers + the TMEM slot (128 B) and the row max / sum
+// exchange between the two softmax halves (2 x 2 x 128 floats).
+constexpr int HEAD_BYTES = 256 + 2 * 2 * QT * 4;
+constexpr int SMEM_BYTES = 232448;  // the per-CTA maximum; the data start is aligned up past HEAD_BYTES
+constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter: keys / output columns split in halves
+constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
+// TMEM columns: S_j in [64*(j&1), +64), O_j in [128 + 64*(j&1), +64),
+// P_j (A operand of P.V, hi then lo) in [256 + 128*(j&1), +128).
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t COL_O = 128, COL_P = 256;
+constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(HD >> 3) << 17) |
+                           (uint32_t(QT >> 4) << 24);  // M=128, N=64 (both products)
+
+struct __align__(64) AttnParams {
+  CUtensorMap q_hi, q_lo, k_hi, k_lo, v_hi, v_lo;  // 4-D {inner, rows, heads, batch}
+  float *O, *O_hi, *O_lo;
+  int64_t ldo, so_b, so_h;
+  int Sq, Sk, heads, tiles_q;
+  float scale;
+  int *err;
+};
+
+enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kSEmpty = 11, kPFull = 13,
+           kPEmpty = 15, kOFull = 17, kOEmpty = 19, kNumBars = 21 };
+
+// D += A(TMEM, 128 x 8, K-major: lane = row, column = k) . B(shared memory).
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accum));
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_constant__ AttnParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + kNumBars);
+  float *xch = reinterpret_cast<float *>(smem_raw + 256);
+  uint8_t *smem =
+      reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + HEAD_BYTES + 1023) & ~uintptr_t(1023));
+  if (smem + DATA_BYTES > smem_raw + SMEM_BYTES) {  // uniform across the CTA: nothing has started yet
+    if (threadIdx.x == 0) atomicCAS(p.err, 0, 99);
+    return;
+  }
+  auto bar = [&](int i) { return smem_u32(bars + i); };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x % p.tiles_q, bh = blockIdx.x / p.tiles_q;
+  const int h = bh % p.heads, b = bh / p.heads;
+  const int q0 = qt * QT;
+  const int nb = (p.Sk + KB - 1) / KB;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kNumBars; i++) {
+      const bool epi = (i == kSEmpty || i == kSEmpty + 1 || i == kPFull || i == kPFull + 1 || i == kOEmpty ||
+                        i == kOEmpty + 1);
+      mbar_init(bar(i), epi ? EPI_WARPS : 1);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t base = smem_u32(smem);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      bool ok = true;
+      mbar_expect_tx(bar(kQFull), Q_BYTES);
+      for (int a = 0; a < 2; a++) {
+        tma_load_4d(base + OFF_Q + a * Q_ATOM, &p.q_hi, bar(kQFull), 32 * a, q0, h, b);
+        tma_load_4d(base + OFF_Q + 2 * Q_ATOM + a * Q_ATOM, &p.q_lo, bar(kQFull), 32 * a, q0, h, b);
+      }
+      auto load_k = [&](int j) {
+        const int s = j & 1;
+        const uint32_t dst = base + OFF_K + s * K_STAGE;
+        mbar_expect_tx(bar(kKFull + s), K_STAGE);
+        for (int a = 0; a < 2; a++) {
+          tma_load_4d(dst + a * K_ATOM, &p.k_hi, bar(kKFull + s), 32 * a, j * KB, h, b);
+          tma_load_4d(dst + 2 * K_ATOM + a * K_ATOM, &p.k_lo, bar(kKFull + s), 32 * a, j * KB, h, b);
+        }
+      };
+      auto load_v = [&](int j) {
+        const int st = j & 1;
+        const uint32_t dst = base + OFF_V + st * V_BYTES;
+        mbar_expect_tx(bar(kVFull + st), V_BYTES);
+        for (int a = 0; a < 2; a++) {
+          tma_load_4d(dst + a * K_ATOM, &p.v_hi, bar(kVFull + st), j * KB + 32 * a, 0, h, b);
+          tma_load_4d(dst + 2 * K_ATOM + a * K_ATOM, &p.v_lo, bar(kVFull + st), j * KB + 32 * a, 0, h, b);
+        }
+      };
+      load_k(0);
+      load_v(0);
+      if (nb > 1) {
+        load_k(1);
+        load_v(1);
+      }
+      for (int j = 0; j + 2 < nb && ok; j++) {
+        if (!mbar_wait(bar(kKEmpty + (j & 1)), (j >> 1) & 1, p.err, 12)) { ok = false; break; }
+        load_k(j + 2);
+        if (!mbar_wait(bar(kVEmpty + (j & 1)), (j >> 1) & 1, p.err, 11)) { ok = false; break; }
+        load_v(j + 2);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(bar(kQFull), 0, p.err, 13);
+      auto pv = [&](int i) {
+        const int u = i & 1;
+        if (!mbar_wait(bar(kPFull + u), (i >> 1) & 1, p.err, 14)) return false;
+        if (!mbar_wait(bar(kVFull + u), (i >> 1) & 1, p.err, 15)) return false;
+        if (i >= 2 && !mbar_wait(bar(kOEmpty + u), ((i >> 1) & 1) ^ 1, p.err, 16)) return false;
+        tc_fence_after();
+        const uint32_t pcol = tmem + COL_P + 128 * u;
+        const uint32_t vbase = base + OFF_V + u * V_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < KB / 8; kk++) {
+          const uint32_t va = vbase + (kk >> 2) * K_ATOM + (kk & 3) * 32;
+          const uint64_t vh = make_desc(va), vl = make_desc(va + 2 * K_ATOM);
+          const uint32_t ph = pcol + 8 * kk, pl = pcol + 64 + 8 * kk;
+          mma_tf32_ts(tmem + COL_O + 64 * u, pl, vh, IDESC, kk == 0 ? 0u : 1u);
+          mma_tf32_ts(tmem + COL_O + 64 * u, ph, vl, IDESC, 1u);
+          mma_tf32_ts(tmem + COL_O + 64 * u, ph, vh, IDESC, 1u);
+        }
+        mma_commit(bar(kVEmpty + u));
+        mma_commit(bar(kPEmpty + u));
+        mma_commit(bar(kOFull + u));
+        return true;
+      };
+      for (int j = 0; j < nb && ok; j++) {
+        const int s = j & 1;
+        if (!mbar_wait(bar(kKFull + s), (j >> 1) & 1, p.err, 17)) { ok = false; break; }
+        if (j >= 2 && !mbar_wait(bar(kSEmpty + s), ((j >> 1) & 1) ^ 1, p.err, 18)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t kbase = base + OFF_K + s * K_STAGE;
+#pragma unroll
+        for (int kk = 0; kk < HD / 8; kk++) {
+          const uint32_t off = (kk & 3) * 32;
+          const uint32_t qa = base + OFF_Q + (kk >> 2) * Q_ATOM + off;
+          const uint32_t ka = kbase + (kk >> 2) * K_ATOM + off;
+          const uint64_t qh = make_desc(qa), ql = make_desc(qa + 2 * Q_ATOM);
+          const uint64_t kh = make_desc(ka), kl = make_desc(ka + 2 * K_ATOM);
+          mma_tf32(tmem + 64 * s, ql, kh, IDESC, kk == 0 ? 0u : 1u);
+          mma_tf32(tmem + 64 * s, qh, kl, IDESC, 1u);
+          mma_tf32(tmem + 64 * s, qh, kh, IDESC, 1u);
+        }
+        mma_commit(bar(kKEmpty + s));
+        mma_commit(bar(kSFull + s));
+        if (j >= 1 && !pv(j - 1)) { ok = false; break; }
+      }
+      if (ok && nb >= 1) pv(nb - 1);
+    }
+  } else {
+    // Softmax warps: thread = query row r of the tile (TMEM lane r); the two
+    // warps of a lane quarter take key / output-column halves hh = 0, 1 and
+    // meet through shared memory (named barrier 1 over the 256 epilogue threads).
+    const int q = warp & 3;
+    const int hh = (warp - 2) >> 2;
+    const int r = 32 * q + lane;
+    float *xmax = xch;                                         // [2][QT]
+    float *xsum = xmax + 2 * QT;                               // [2][QT]
+    const uint32_t lane_base = tmem + (uint32_t(32 * q) << 16);
+    constexpr int HK = KB / 2, HO = HD / 2;
+    float o[HO];
+#pragma unroll
+    for (int i = 0; i < HO; i++) o[i] = 0.0f;
+    float m = __int_as_float(0xff800000), l = 0.0f, corr_prev = 1.0f;
+    bool ok = true;
+    for (int j = 0; j < nb; j++) {
+      const int s = j & 1;
+      bool w = mbar_wait(bar(kSFull + s), (j >> 1) & 1, p.err, 19);
+      if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+      tc_fence_after();
+      float sc[HK];
+      {
+        uint32_t r0[32];
+        tmem_ld32_nowait(lane_base + 64 * s + HK * hh, r0);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < HK; i++) sc[i] = __uint_as_float(r0[i]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kSEmpty + s));
+      float mj = __int_as_float(0xff800000);
+#pragma unroll
+      for (int i = 0; i < HK; i++) {
+        float x = __fmul_rn(sc[i], p.scale);           // the reference's `* scale` node
+        if (j * KB + HK * hh + i >= p.Sk) x = __int_as_float(0xff800000);
+        sc[i] = x;
+        mj = fmaxf(mj, x);
+      }
+      xmax[hh * QT + r] = mj;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      const float m_new = fmaxf(m, fmaxf(xmax[r], xmax[QT + r]));
+      const float corr = (m == m_new) ? 1.0f : expf(__fsub_rn(m, m_new));
+      float ps = 0.0f;
+#pragma unroll
+      for (int i = 0; i < HK; i++) {
+        const float e = expf(__fsub_rn(sc[i], m_new));
+        sc[i] = e;
+        ps += e;
+      }
+      xsum[hh * QT + r] = ps;
+      m = m_new;
+      // P_j (this half's 32 keys), split, into TMEM buffer j & 1 once P.V of
+      // block j - 2 has finished reading it.
+      if (j >= 2) {
+        bool w3 = mbar_wait(bar(kPEmpty + s), ((j >> 1) & 1) ^ 1, p.err, 22);
+        if (!__all_sync(0xffffffffu, w3)) { ok = false; break; }
+        tc_fence_after();
+      }
+      {
+        uint32_t hv[32], lv[32];
+#pragma unroll
+        for (int i = 0; i < HK; i++) {
+          const float hx = tf32_rna(sc[i]);
+          hv[i] = __float_as_uint(hx);
+          lv[i] = __float_as_uint(__fsub_rn(sc[i], hx));
+        }
+        const uint32_t pcol = lane_base + COL_P + 128 * s + HK * hh;
+        tmem_st32(pcol, hv);
+        tmem_st32(pcol + 64, lv);
+        tmem_st_wait();
+      }
+      tc_fence_before();
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      l = __fadd_rn(__fmul_rn(l, corr), __fadd_rn(xsum[r], xsum[QT + r]));
+      if (lane == 0) mbar_arrive(bar(kPFull + s));
+      if (j >= 1) {  // fold O_{j-1} (relative to the previous max) into o
+        const int u = (j - 1) & 1;
+        bool w2 = mbar_wait(bar(kOFull + u), ((j - 1) >> 1) & 1, p.err, 20);
+        if (!__all_sync(0xffffffffu, w2)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t r0[32];
+        tmem_ld32_nowait(lane_base + COL_O + 64 * u + HO * hh, r0);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(kOEmpty + u));
+#pragma unroll
+        for (int i = 0; i < HO; i++) o[i] = __fadd_rn(__fmul_rn(o[i], corr_prev), __uint_as_float(r0[i]));
+      }
+      corr_prev = corr;
+    }
+    if (ok && nb >= 1) {
+      const int u = (nb - 1) & 1;
+      bool w = mbar_wait(bar(kOFull + u), ((nb - 1) >> 1) & 1, p.err, 21);
+      if (__all_sync(0xffffffffu, w)) {
+        tc_fence_after();
+        uint32_t r0[32];
+        tmem_ld32_nowait(lane_base + COL_O + 64 * u + HO * hh, r0);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < HO; i++) o[i] = __fadd_rn(__fmul_rn(o[i], corr_prev), __uint_as_float(r0[i]));
+        const int row = q0 + r;
+        if (row < p.Sq && *reinterpret_cast<volatile int *>(p.err) == 0) {
+          const float inv = __frcp_rn(l);
+          const int64_t off = int64_t(b) * p.so_b + int64_t(h) * p.so_h + int64_t(row) * p.ldo + HO * hh;
+#pragma unroll
+          for (int c = 0; c < HO; c += 4) {
+            float4 v = make_float4(__fmul_rn(o[c], inv), __fmul_rn(o[c + 1], inv), __fmul_rn(o[c + 2], inv),
+                                   __fmul_rn(o[c + 3], inv));
+            if (p.O) *reinterpret_cast<float4 *>(p.O + off + c) = v;
+            if (p.O_hi) {
+              float4 hv = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
+              *reinterpret_cast<float4 *>(p.O_hi + off + c) = hv;
+              *reinterpret_cast<float4 *>(p.O_lo + off + c) =
+                  make_float4(__fsub_rn(v.x, hv.x), __fsub_rn(v.y, hv.y), __fsub_rn(v.z, hv.z), __fsub_rn(v.w, hv.w));
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+  }
+}
+
+bool view_ok(const void *p, int64_t ld, int64_t sb, int64_t sh) {
+  return p && aligned16(p) && ld % 4 == 0 && sb % 4 == 0 && sh % 4 == 0;
+}
+
+}  // namespace
+}  // namespace silcu
+
+using namespace silcu;
+
+extern "C" silcu_status silcu_attention_f32(const silcu_attention_args *ap, silcu_stream stream) {
+  if (!ap) return fail(SILCU_INVALID_ARGUMENT, "attention: null args");
+  const silcu_attention_args &a = *ap;
+  if (a.D != HD) return fail(SILCU_UNSUPPORTED, "attention: head dimension %lld (only 64)", (long long)a.D);
+  if (a.Sq <= 0 || a.Sk <= 0 || a.batch <= 0 || a.heads <= 0)
+    return fail(SILCU_INVALID_ARGUMENT, "attention: empty extent");
+  if (!(view_ok(a.Q_hi, a.ldq, a.sq_b, a.sq_h) && view_ok(a.Q_lo, a.ldq, a.sq_b, a.sq_h) &&
+        view_ok(a.K_hi, a.ldk, a.sk_b, a.sk_h) && view_ok(a.K_lo, a.ldk, a.sk_b, a.sk_h) &&
+        view_ok(a.Vt_hi, a.ldv, a.sv_b, a.sv_h) && view_ok(a.Vt_lo, a.ldv, a.sv_b, a.sv_h)))
+    return fail(SILCU_INVALID_ARGUMENT, "attention: operands need 16-byte aligned rows and strides");
+  const bool split_out = a.O_hi && a.O_lo;
+  if (!a.O && !split_out) return fail(SILCU_INVALID_ARGUMENT, "attention: no output");
+  if ((a.O && !view_ok(a.O, a.ldo, a.so_b, a.so_h)) ||
+      (split_out && !(view_ok(a.O_hi, a.ldo, a.so_b, a.so_h) && view_ok(a.O_lo, a.ldo, a.so_b, a.so_h))))
+    return fail(SILCU_INVALID_ARGUMENT, "attention: output needs 16-byte aligned rows and strides");
+  const int64_t tiles_q = (a.Sq + QT - 1) / QT;
+  if (tiles_q * a.heads * a.batch > 0x7FFFFFFF || a.Sq > (1 << 30) || a.Sk > (1 << 30))
+    return fail(SILCU_UNSUPPORTED, "attention: too large");
+  AttnParams p;
+  memset(&p, 0, sizeof(p));
+  if (!make_map4(&p.q_hi, a.Q_hi, HD, a.Sq, a.ldq, a.heads, a.sq_h, a.batch, a.sq_b, 32, QT) ||
+      !make_map4(&p.q_lo, a.Q_lo, HD, a.Sq, a.ldq, a.heads, a.sq_h, a.batch, a.sq_b, 32, QT) ||
+      !make_map4(&p.k_hi, a.K_hi, HD, a.Sk, a.ldk, a.heads, a.sk_h, a.batch, a.sk_b, 32, KB) ||
+      !make_map4(&p.k_lo, a.K_lo, HD, a.Sk, a.ldk, a.heads, a.sk_h, a.batch, a.sk_b, 32, KB) ||
+      !make_map4(&p.v_hi, a.Vt_hi, a.Sk, HD, a.ldv, a.heads, a.sv_h, a.batch, a.sv_b, 32, HD) ||
+      !make_map4(&p.v_lo, a.Vt_lo, a.Sk, HD, a.ldv, a.heads, a.sv_h, a.batch, a.sv_b, 32, HD))
+    return fail(SILCU_CUDA_ERROR, "attention: cuTensorMapEncodeTiled failed");
+  p.O = a.O;
+  p.O_hi = split_out ? a.O_hi : nullptr;
+  p.O_lo = split_out ? a.O_lo : nullptr;
+  p.ldo = a.ldo;
+  p.so_b = a.so_b;
+  p.so_h = a.so_h;
+  p.Sq = int(a.Sq);
+  p.Sk = int(a.Sk);
+  p.heads = int(a.heads);
+  p.tiles_q = int(tiles_q);
+  p.scale = a.scale;
+  p.err = device_error_ptr();
+  if (!p.err) return fail(SILCU_CUDA_ERROR, "attention: no device error word");
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return fail(SILCU_CUDA_ERROR, "attention: smem attribute: %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  attn_kernel<<<uint32_t(tiles_q * a.heads * a.batch), NUM_THREADS, SMEM_BYTES, as_stream(stream)>>>(p);
+  return check_launch("attention");
+}

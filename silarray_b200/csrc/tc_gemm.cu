@@ -30,9 +30,11 @@
 
 #include "common.cuh"
 #include "gemm_internal.cuh"
+#include "tc_common.cuh"
 
 namespace silcu {
 namespace {
+using namespace tc;
 
 constexpr int BM = 128, BK = 32;
 
@@ -62,7 +64,6 @@ struct Cfg {
 };
 constexpr int CHUNK_KB_DEFAULT = 4;      // K blocks per TMEM accumulation chunk
 constexpr int GROUP_M = 8;
-constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s per wait
 
 struct TcEpi {
   float alpha;
@@ -83,133 +84,6 @@ struct __align__(64) TcParams {
   TcEpi epi;
   int *err;
 };
-
-// ----------------------------------------------------------------- PTX glue
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ unsigned long long globaltimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait.  Returns false (and records `code`) when the phase does not
-// complete within WAIT_NS, or when another CTA already recorded an error.
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *err, int code) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer();
-  for (uint32_t i = 1;; i++) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0) {
-      if (*reinterpret_cast<volatile int *>(err) != 0) return false;
-      if (globaltimer() - t0 > WAIT_NS) {
-        atomicCAS(err, 0, code);
-        return false;
-      }
-    }
-  }
-}
-
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0, int c1,
-                                            int c2, int c3) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-      : "memory");
-}
-
-// TMA store of one 32x32 fp32 box from shared memory (bulk-group completion).
-__device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, uint32_t src, int c0, int c1, int c2, int c3) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
-          reinterpret_cast<uint64_t>(map)),
-      "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-      : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-__device__ __forceinline__ float tf32_rna(float x) {
-  uint32_t h;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
-  return __uint_as_float(h);
-}
-
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-// Shared-memory matrix descriptor, K-major operand with 128-byte swizzle:
-// 8-row x 128-byte swizzle atoms stacked along M/N every 1024 bytes (SBO);
-// LBO is unused for this layout (encoded as 1); version 1 (sm_100).
-__device__ __forceinline__ uint64_t make_desc(uint32_t addr) {
-  uint64_t d = 0;
-  d |= uint64_t((addr & 0x3FFFFu) >> 4);
-  d |= uint64_t(1) << 16;
-  d |= uint64_t(1024 >> 4) << 32;
-  d |= uint64_t(1) << 46;
-  d |= uint64_t(2) << 61;
-  return d;
-}
-
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accum) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum));
-}
-
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
-        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
-        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 struct Tile {
   int bz, m0, n0;
@@ -233,9 +107,6 @@ __device__ __forceinline__ Tile decode_tile(const TcParams &p, int idx) {
   return r;
 }
 
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
 
 // Writes a lane's 32 values (its row of a 32x32 block) into the warp's 4 KB
 // staging block in the TMA 128-byte-swizzle layout: 16-byte chunk j of row r
@@ -572,46 +443,6 @@ __global__ void __launch_bounds__(256) split_contig(const float *__restrict__ sr
 }
 
 // ---------------------------------------------------------------- host side
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
-    void *ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  }
-  return fn;
-}
-
-// A 4-D fp32 view {inner, rows, bin, bout} with element strides {1, ld, s_in,
-// s_out}, boxes {box0, box1, 1, 1}, 128-byte swizzle.  Strides of extent-1
-// dimensions are replaced by a valid dummy.
-bool make_map4(CUtensorMap *m, const float *base, int64_t inner, int64_t rows, int64_t ld, int64_t bin,
-               int64_t s_in, int64_t bout, int64_t s_out, int box0, int box1) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return false;
-  const int64_t span = ld * rows;
-  if (bin <= 1) s_in = span;
-  if (bout <= 1) s_out = s_in * (bin > 1 ? bin : 1);
-  cuuint64_t dims[4] = {cuuint64_t(inner), cuuint64_t(rows), cuuint64_t(bin), cuuint64_t(bout)};
-  cuuint64_t strides[3] = {cuuint64_t(ld) * 4, cuuint64_t(s_in) * 4, cuuint64_t(s_out) * 4};
-  cuuint32_t box[4] = {cuuint32_t(box0), cuuint32_t(box1), 1, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float *>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
-bool aligned_view(const void *p, int64_t ld, int64_t s_in, int64_t s_out) {
-  return p && aligned16(p) && ld % 4 == 0 && s_in % 4 == 0 && s_out % 4 == 0 && ld > 0;
-}
-
 int64_t padded_k(int64_t K) { return ((K + BK - 1) / BK) * BK; }
 
 template <int BN>
@@ -777,4 +608,20 @@ extern "C" silcu_status silcu_split_f32(const float *src, size_t rows, size_t co
   dim3 g(uint32_t((K + 31) / 32), uint32_t((R + 31) / 32), 1);
   pack_split<<<g, 256, 0, as_stream(stream)>>>(src, nullptr, rs, ks, 0, 1, 0, R, K, K, hi, lo);
   return check_launch("split");
+}
+
+extern "C" silcu_status silcu_transpose_split_f32(const float *src, const float *src_lo, size_t rows, size_t cols,
+                                                  size_t ld, size_t batch, size_t heads, size_t s_b, size_t s_h,
+                                                  float *hi, float *lo, silcu_stream stream) {
+  using namespace silcu;
+  if (rows == 0 || cols == 0 || batch == 0 || heads == 0) return SILCU_OK;
+  if (!src || !hi || !lo || ld < cols) return fail(SILCU_INVALID_ARGUMENT, "transpose_split: bad argument");
+  if (rows > 65535ull * 32 || cols > 65535ull * 32 || batch * heads > 65535)
+    return fail(SILCU_UNSUPPORTED, "transpose_split: extent too large");
+  // output block (b, h) is [cols, rows]: element (c, r) = src[b*s_b + h*s_h + r*ld + c]
+  const int64_t R = int64_t(cols), K = int64_t(rows);
+  dim3 g(uint32_t((K + 31) / 32), uint32_t((R + 31) / 32), uint32_t(batch * heads));
+  pack_split<<<g, 256, 0, as_stream(stream)>>>(src, src_lo, 1, int64_t(ld), int64_t(s_b), int64_t(heads),
+                                               int64_t(s_h), R, K, K, hi, lo);
+  return check_launch("transpose_split");
 }

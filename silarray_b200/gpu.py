@@ -257,6 +257,46 @@ def split(src, rows, cols, ld=None, transpose=False):
     return hi, lo
 
 
+def transpose_split(src, rows, cols, ld, batch=1, heads=1, s_b=0, s_h=0, src_lo=None, out=None):
+    """(hi, lo) of the per-(b, h) transposes of [rows, cols] blocks (see silcu_transpose_split_f32)."""
+    _dev(src, _F32)
+    n = batch * heads * rows * cols
+    if out is None:
+        hi = torch.empty(n, dtype=_F32, device=src.device)
+        lo = torch.empty(n, dtype=_F32, device=src.device)
+    else:
+        hi, lo = _dev(out[0], _F32), _dev(out[1], _F32)
+    check(lib().silcu_transpose_split_f32(_p(src), _p(src_lo), rows, cols, ld, batch, heads, s_b, s_h,
+                                          _p(hi), _p(lo), _stream()))
+    return hi, lo
+
+
+def attention(Q, K, Vt, *, Sq, Sk, batch, heads, ldq, sq_b, sq_h, ldk, sk_b, sk_h, ldv, sv_b, sv_h,
+              scale, O=None, O_split=None, ldo=None, so_b=None, so_h=None, D=64):
+    """Fused softmax(Q.K^T * scale).V; Q, K, Vt are (hi, lo) split pairs."""
+    a = _lib.AttnArgs()
+    for nm, pair in (("Q", Q), ("K", K), ("Vt", Vt)):
+        _dev(pair[0], _F32), _dev(pair[1], _F32)
+        setattr(a, nm + "_hi", pair[0].data_ptr())
+        setattr(a, nm + "_lo", pair[1].data_ptr())
+    if O is None and O_split is None:
+        O = torch.empty(batch * heads * Sq * D, dtype=_F32, device=Q[0].device)
+    if O is not None:
+        a.O = _dev(O, _F32).data_ptr()
+    if O_split is not None:
+        a.O_hi, a.O_lo = _dev(O_split[0], _F32).data_ptr(), _dev(O_split[1], _F32).data_ptr()
+    a.Sq, a.Sk, a.D, a.batch, a.heads = Sq, Sk, D, batch, heads
+    a.ldq, a.sq_b, a.sq_h = ldq, sq_b, sq_h
+    a.ldk, a.sk_b, a.sk_h = ldk, sk_b, sk_h
+    a.ldv, a.sv_b, a.sv_h = ldv, sv_b, sv_h
+    a.ldo = D if ldo is None else ldo
+    a.so_h = Sq * D if so_h is None else so_h
+    a.so_b = heads * Sq * D if so_b is None else so_b
+    a.scale = float(scale)
+    check(lib().silcu_attention_f32(ct.byref(a), _stream()))
+    return O
+
+
 def argmax_f32(IN, OUT=None, rows=None, cols=None):
     _dev(IN, _F32)
     rows, cols = (IN.shape[0], IN.shape[-1]) if rows is None else (rows, cols)

@@ -13,10 +13,11 @@ rounding sequence per element is the reference's (dot, then + bias, then
 act, then + residual).  Q, K and V come from one GEMM against [Wq|Wk|Wv]
 (columns are independent, so the values equal three separate GEMMs).
 
-Launches per forward: layer_norm, QKV gemm, scores gemm (batched over
-sequence x head with strided views), softmax, V re-split + context gemm, Wo
-gemm (+bias +residual), layer_norm, W1 gemm (+bias, relu), W2 gemm (+bias
-+residual).  Every GEMM is the 3xTF32 tcgen05 kernel.
+Launches per forward: layer_norm, QKV gemm, V^T split, fused attention
+(scores, softmax and the context product in one tcgen05 kernel, per
+sequence x head through strided views), Wo gemm (+bias +residual),
+layer_norm, W1 gemm (+bias, relu), W2 gemm (+bias +residual).  Every
+product is 3xTF32 on tcgen05.
 """
 from dataclasses import dataclass
 
@@ -112,8 +113,7 @@ class Block:
         pair = lambda n: (e(n), e(n))  # noqa: E731
         self.h = pair(T * d)
         self.qkv = pair(T * 3 * d)
-        self.scores = e(cfg.batch * H * S * S)
-        self.p = pair(cfg.batch * H * S * S)
+        self.vt = pair(cfg.batch * H * cfg.head_dim * S)
         self.ctx = pair(T * d)
         self.r1 = e(T * d)
         self.ff = pair(T * f)
@@ -128,17 +128,14 @@ class Block:
         gpu.layer_norm_split(x, self.g1, self.be1, T, d, cfg.eps, *self.h)
         gpu.gemm(self.h, self.wqkv_t, M=T, N=3 * d, K=d, trans_b=True, bias=self.bqkv,
                  no_c=True, C_split=self.qkv)
-        # scores[b, h] = Q_bh . K_bh^T * scale   (Q_bh rows: qkv[b*S + s, h*hd : h*hd+hd])
-        gpu.gemm((qh, ql), (qh[d:], ql[d:]), self.scores, M=S, N=S, K=hd, lda=3 * d, ldb=3 * d,
-                 trans_b=True, batch=B, stride_a=S * 3 * d, stride_b=S * 3 * d, stride_c=H * S * S,
-                 batch_inner=H, stride_a_inner=hd, stride_b_inner=hd, stride_c_inner=S * S,
-                 alpha=self.scale)
-        gpu.softmax_split(self.scores, B * H * S, S, *self.p)
-        # ctx[b*S + s, h*hd + j] = (attn_bh . V_bh)[s, j]
-        gpu.gemm(self.p, (qh[2 * d:], ql[2 * d:]), M=S, N=hd, K=S, lda=S, ldb=3 * d, ldc=d,
-                 batch=B, stride_a=H * S * S, stride_b=S * 3 * d, stride_c=S * d,
-                 batch_inner=H, stride_a_inner=S * S, stride_b_inner=hd, stride_c_inner=hd,
-                 no_c=True, C_split=self.ctx)
+        # ctx[b*S + s, h*hd + j] = softmax(Q_bh . K_bh^T * scale) . V_bh, fused; Q_bh rows are
+        # qkv[b*S + s, h*hd : h*hd + hd], K_bh the same at +d; V_bh^T comes split and transposed.
+        gpu.transpose_split(qh[2 * d:], S, hd, 3 * d, batch=B, heads=H, s_b=S * 3 * d, s_h=hd,
+                            src_lo=ql[2 * d:], out=self.vt)
+        gpu.attention((qh, ql), (qh[d:], ql[d:]), self.vt, Sq=S, Sk=S, batch=B, heads=H,
+                      ldq=3 * d, sq_b=S * 3 * d, sq_h=hd, ldk=3 * d, sk_b=S * 3 * d, sk_h=hd,
+                      ldv=S, sv_b=H * hd * S, sv_h=hd * S, scale=self.scale,
+                      O_split=self.ctx, ldo=d, so_b=S * d, so_h=hd)
         gpu.gemm(self.ctx, self.wo_t, self.r1, M=T, N=d, K=d, trans_b=True, bias=self.bo, residual=x)
         gpu.layer_norm_split(self.r1, self.g2, self.be2, T, d, cfg.eps, *self.h)
         gpu.gemm(self.h, self.w1_t, M=T, N=f, K=d, trans_b=True, bias=self.b1, act="relu",

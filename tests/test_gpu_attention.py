@@ -1,0 +1,44 @@
+"""Fused attention (silcu_attention_f32) vs the node-by-node oracle chain:
+scores = fl(Q.K^T * scale) (fp64-accumulated GEMM), softmax (the reference's
+CPU softmax), O = P.V; tolerance |g - r| <= sqrt(Sk) * (1e-6 + 1e-5 |r|)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from silarray_b200 import gpu
+from tests._tol import assert_dot_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(q, k, v, scale):
+    s = O.scalar_op("mul", scale, O.sgemm(q, k, tb=True)).reshape(q.shape[0], k.shape[0])
+    return O.sgemm(O.softmax(s), v)
+
+
+@pytest.mark.parametrize("B,H,S", [(1, 1, 64), (2, 3, 200), (1, 2, 512), (1, 1, 1000)])
+def test_attention_matches_chain(cuda, B, H, S):
+    D = 64
+    rng = np.random.default_rng(S + H)
+    q = rng.normal(0, 1, (B, H, S, D)).astype(np.float32)
+    k = rng.normal(0, 1, (B, H, S, D)).astype(np.float32)
+    v = rng.normal(0, 1, (B, H, S, D)).astype(np.float32)
+    dq, dk, dv = (torch.from_numpy(t).cuda().reshape(-1) for t in (q, k, v))
+    qs = gpu.split(dq, B * H * S, D)
+    ks = gpu.split(dk, B * H * S, D)
+    vt = gpu.transpose_split(dv, S, D, D, batch=B, heads=H, s_b=H * S * D, s_h=S * D)
+    scale = float(np.float32(0.125))
+    hi = torch.empty(B * H * S * D, device="cuda")
+    lo = torch.empty(B * H * S * D, device="cuda")
+    out = gpu.attention(qs, ks, vt, Sq=S, Sk=S, batch=B, heads=H, ldq=D, sq_b=H * S * D, sq_h=S * D,
+                        ldk=D, sk_b=H * S * D, sk_h=S * D, ldv=S, sv_b=H * D * S, sv_h=D * S,
+                        scale=scale, O_split=(hi, lo), O=torch.empty(B * H * S * D, device="cuda"))
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().reshape(B, H, S, D)
+    np.testing.assert_array_equal((hi + lo).cpu().numpy().reshape(B, H, S, D), got)
+    for b in range(B):
+        for h in range(H):
+            assert_dot_close(got[b, h], _ref(q[b, h], k[b, h], v[b, h], np.float32(scale)), S,
+                             what=f"attention b{b} h{h}")
+    gpu.device_status()
