@@ -3,11 +3,14 @@
 //   ffma_gemm   128x128x8 tiles, 256 threads, 8x8 outputs per thread, fp32
 //               FFMA.  Handles every stride/transpose/batch/tail case and is
 //               the accuracy reference for the tensor-core path.
-//   skinny_gemm M <= 16 rows per CTA (GEMV at M = 1): each thread streams
-//               float4 columns of W with K split across warps and CTAs, so W
-//               is read from HBM once; partials are combined in a fixed order.
+//   skinny_gemm M <= 64 (GEMV at M = 1): each thread streams 2-4 columns of
+//               W with K split across warps and CTAs, so W is read from HBM
+//               once; partials are combined in a fixed order.
 //   tensor-core 3xTF32 tcgen05 path lives in tc_gemm.cu.
+#include <stdlib.h>
 #include <string.h>
+
+#include <cooperative_groups.h>
 
 #include "common.cuh"
 #include "gemm_internal.cuh"
@@ -145,148 +148,388 @@ __global__ void __launch_bounds__(256) ffma_gemm(const FfmaArgs p) {
 }
 
 // ------------------------------------------------------- skinny GEMM / GEMV
-// CTA = 8 warps over one 128-column tile; lane l owns columns 4l..4l+3.
-// Warps split the CTA's K chunk round-robin; CTAs (grid.y) split K further.
-// Each thread keeps MR float4 accumulators (MR rows of X).
-template <int MR>
-__global__ void __launch_bounds__(256) skinny_gemm(const float *__restrict__ X, int64_t ldx,
-                                                   const float *__restrict__ W, int64_t ldw,
-                                                   float *__restrict__ out, int64_t ldo, int64_t M,
-                                                   int64_t N, int64_t K, int64_t kchunk,
-                                                   float *__restrict__ part, Epi epi) {
-  __shared__ float red[MR][128];
-  extern __shared__ float xs[];  // [MR][kchunk]
+// HBM-bound: W is streamed once.  A CTA (8 warps) owns a tile of 32*CPL
+// columns (lane l holds CPL consecutive columns), MR rows of X and one K
+// slice; its warps take the slice's k round-robin with UNROLL W loads in
+// flight per thread, the first batch issued before X's slice is staged
+// (transposed, [k][m], so the MR values of one k are broadcast loads).  The
+// K slices of a tile run as one 8-CTA cluster and are combined through
+// distributed shared memory in rank order; with more than 8 slices per tile,
+// G cluster groups write partials that skinny_finish adds in group order.
+// Every sum has a fixed order, so results are deterministic.
+constexpr int kSkinnyCluster = 8;
+constexpr int kSkinnyMaxChunk = 256;  // K per CTA at most
+
+template <int MR, int CPL, int UNROLL>
+__global__ void __cluster_dims__(1, kSkinnyCluster, 1) __launch_bounds__(256, MR <= 8 ? 4 : 1)
+    skinny_gemm(const float *__restrict__ X, int64_t ldx, const float *__restrict__ W, int64_t ldw,
+                float *__restrict__ out, int64_t ldo, int64_t M, int64_t N, int64_t K, int64_t kchunk,
+                float *__restrict__ part, Epi epi) {
+  namespace cg = cooperative_groups;
+  constexpr int COLS = 32 * CPL, E = MR * COLS;
+  extern __shared__ float4 smem4[];
+  float *wred = reinterpret_cast<float *>(smem4);  // [8][E] per-warp sums
+  float *red = wred + 8 * E;                       // [E] CTA sum (read by the cluster)
+  float *xs = red + E;                             // [kchunk][MR]
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t col0 = int64_t(blockIdx.x) * COLS;
+  const int64_t c0 = col0 + lane * CPL;
+  const int64_t k0 = int64_t(blockIdx.y) * kchunk;
+  const int64_t kend = k0 + kchunk < K ? k0 + kchunk : K;
+  const int kn = kend > k0 ? int(kend - k0) : 0;
+  const int64_t m0 = int64_t(blockIdx.z) * MR;
+  const bool full = c0 + CPL <= N && ((reinterpret_cast<uintptr_t>(W + c0) & (4 * CPL - 1)) == 0);
+  auto loadw = [&](int kk, float (&wv)[CPL]) {
+    if (kk >= kn) {
+#pragma unroll
+      for (int c = 0; c < CPL; c++) wv[c] = 0.0f;
+      return;
+    }
+    const float *src = W + (k0 + kk) * ldw + c0;
+    if (full) {
+      if constexpr (CPL == 4) {
+        const float4 f = __ldg(reinterpret_cast<const float4 *>(src));
+        wv[0] = f.x; wv[1] = f.y; wv[2] = f.z; wv[3] = f.w;
+      } else if constexpr (CPL == 2) {
+        const float2 f = __ldg(reinterpret_cast<const float2 *>(src));
+        wv[0] = f.x; wv[1] = f.y;
+      } else {
+        wv[0] = __ldg(src);
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < CPL; c++) wv[c] = c0 + c < N ? src[c] : 0.0f;
+    }
+  };
+  float acc[MR][CPL];
+#pragma unroll
+  for (int r = 0; r < MR; r++)
+#pragma unroll
+    for (int c = 0; c < CPL; c++) acc[r][c] = 0.0f;
+  auto fma_row = [&](int kk, const float (&wv)[CPL]) {
+    const float *xr = xs + kk * MR;
+    constexpr int V = MR >= 4 ? 4 : 1;
+#pragma unroll
+    for (int r = 0; r < MR; r += V) {
+      float xv[4];
+      if constexpr (V == 4) {
+        const float4 f = *reinterpret_cast<const float4 *>(xr + r);
+        xv[0] = f.x; xv[1] = f.y; xv[2] = f.z; xv[3] = f.w;
+      } else {
+        xv[0] = xr[r];
+      }
+#pragma unroll
+      for (int q = 0; q < V; q++)
+#pragma unroll
+        for (int c = 0; c < CPL; c++) acc[r + q][c] = fmaf(xv[q], wv[c], acc[r + q][c]);
+    }
+  };
+  // First W batch in flight while X's slice is staged.
+  float wv[UNROLL][CPL];
+#pragma unroll
+  for (int u = 0; u < UNROLL; u++) loadw(w + 8 * u, wv[u]);
+  // X slice: thread e loads 4 consecutive k of row e % MR (16-byte loads when
+  // aligned), XB loads in flight per thread; the [k][m] stores of a warp hit
+  // consecutive rows, so they are free of bank conflicts.
+  {
+    constexpr int XB = 8;
+    const int k4n = int(kchunk) / 4;  // the whole slice, zero past kn
+    const bool xvec = (ldx % 4) == 0 && (reinterpret_cast<uintptr_t>(X) & 15) == 0;
+    for (int base = threadIdx.x; base < MR * k4n; base += 256 * XB) {
+      float v[XB][4];
+#pragma unroll
+      for (int u = 0; u < XB; u++) {
+        const int e = base + u * 256, r = e % MR, kk = (e / MR) * 4;
+        const float *src = X + (m0 + r) * ldx + k0 + kk;
+        if (e < MR * k4n && m0 + r < M) {
+          if (xvec && kk + 4 <= kn) {
+            const float4 f = __ldg(reinterpret_cast<const float4 *>(src));
+            v[u][0] = f.x; v[u][1] = f.y; v[u][2] = f.z; v[u][3] = f.w;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 4; i++) v[u][i] = kk + i < kn ? src[i] : 0.0f;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; i++) v[u][i] = 0.0f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < XB; u++) {
+        const int e = base + u * 256, r = e % MR, kk = (e / MR) * 4;
+        if (e < MR * k4n)
+#pragma unroll
+          for (int i = 0; i < 4; i++) xs[(kk + i) * MR + r] = v[u][i];
+      }
+    }
+  }
+  __syncthreads();
+  // kchunk is a multiple of 8 * UNROLL and X's slice is zero past kn, so the
+  // loop needs no guards (W loads past kn return 0).
+  for (int kk = w; kk < kchunk; kk += 8 * UNROLL) {
+    if (kk > w) {
+#pragma unroll
+      for (int u = 0; u < UNROLL; u++) loadw(kk + 8 * u, wv[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < UNROLL; u++) fma_row(kk + 8 * u, wv[u]);
+  }
+#pragma unroll
+  for (int r = 0; r < MR; r++)
+#pragma unroll
+    for (int c = 0; c < CPL; c++) wred[w * E + r * COLS + lane * CPL + c] = acc[r][c];
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += 256) {
+    float v = wred[e];
+#pragma unroll
+    for (int ww = 1; ww < 8; ww++) v += wred[ww * E + e];
+    red[e] = v;
+  }
+  cg::cluster_group cl = cg::this_cluster();
+  cl.sync();
+  // Rank q of the cluster finishes elements [q*E/8, (q+1)*E/8) of the tile.
+  const int q = int(cl.block_rank());
+  const int64_t g = blockIdx.y / kSkinnyCluster;
+  for (int e = q * (E / kSkinnyCluster) + threadIdx.x; e < (q + 1) * (E / kSkinnyCluster); e += 256) {
+    float v = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kSkinnyCluster; j++) v += cl.map_shared_rank(red, j)[e];
+    const int r = e / COLS, c = e % COLS;
+    const int64_t row = m0 + r, col = col0 + c;
+    if (row >= M || col >= N) continue;
+    if (part) part[(g * M + row) * N + col] = v;
+    else out[row * ldo + col] = apply_epi(epi, v, row, col);
+  }
+  cl.sync();  // peers' shared memory stays valid until every rank has read it
+}
+
+// GEMV (M = 1): a CTA owns 128 columns (lane l holds 4, float4 loads) and a
+// slice of K; warp w takes rows w, w+8, ... of the slice, GEMV_UNROLL float4
+// loads in flight per thread from a pointer stepped by 8 rows.  x is read
+// through the read-only cache (one broadcast per warp and row).  The 8 warps
+// combine in warp order in shared memory, then the CL consecutive slices of a
+// cluster combine in rank order through distributed shared memory; with more
+// than CL slices, each cluster writes a partial that skinny_finish adds in
+// order.
+constexpr int kGemvUnroll = 8;
+
+__global__ void __launch_bounds__(256, 4) gemv_kernel(const float *__restrict__ x, const float *__restrict__ W,
+                                                   int64_t ldw, float *__restrict__ out, int64_t N, int64_t K,
+                                                   int64_t kchunk, float *__restrict__ part, Epi epi) {
+  namespace cg = cooperative_groups;
+  __shared__ float4 wsum[8][32];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int64_t c0 = int64_t(blockIdx.x) * 128 + lane * 4;
   const int64_t k0 = int64_t(blockIdx.y) * kchunk;
   const int64_t k1 = k0 + kchunk < K ? k0 + kchunk : K;
-  const int64_t m0 = int64_t(blockIdx.z) * MR;
-  const int kn = int(k1 - k0);
-  for (int e = threadIdx.x; e < MR * kn; e += 256) {
-    const int r = e / kn, kk = e % kn;
-    xs[r * kchunk + kk] = (m0 + r < M) ? X[(m0 + r) * ldx + k0 + kk] : 0.0f;
-  }
-  for (int e = threadIdx.x; e < MR * 128; e += 256) red[e / 128][e % 128] = 0.0f;
-  __syncthreads();
-  float4 acc[MR];
+  const bool vec = c0 + 4 <= N;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float *p = W + (k0 + w) * ldw + c0;
+  const int64_t step = 8 * ldw;
+  int64_t k = k0 + w;
+  for (; k + 8 * (kGemvUnroll - 1) < k1; k += 8 * kGemvUnroll) {
+    float4 wv[kGemvUnroll];
+    float xv[kGemvUnroll];
+    if (vec) {
 #pragma unroll
-  for (int r = 0; r < MR; r++) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-  const bool full = c0 + 4 <= N;
-  int kk = w;
-  for (; kk + 24 < kn; kk += 32) {
-    float4 wv[4];
+      for (int u = 0; u < kGemvUnroll; u++) wv[u] = __ldg(reinterpret_cast<const float4 *>(p + u * step));
+    } else {
 #pragma unroll
-    for (int u = 0; u < 4; u++) {
-      const float *src = W + (k0 + kk + u * 8) * ldw + c0;
-      if (full) wv[u] = __ldg(reinterpret_cast<const float4 *>(src));
-      else {
-        wv[u].x = c0 < N ? src[0] : 0.f; wv[u].y = c0 + 1 < N ? src[1] : 0.f;
-        wv[u].z = c0 + 2 < N ? src[2] : 0.f; wv[u].w = c0 + 3 < N ? src[3] : 0.f;
+      for (int u = 0; u < kGemvUnroll; u++) {
+        const float *q = p + u * step;
+        wv[u] = make_float4(c0 < N ? q[0] : 0.f, c0 + 1 < N ? q[1] : 0.f, c0 + 2 < N ? q[2] : 0.f, 0.f);
       }
     }
 #pragma unroll
-    for (int u = 0; u < 4; u++)
+    for (int u = 0; u < kGemvUnroll; u++) xv[u] = __ldg(x + k + 8 * u);
 #pragma unroll
-      for (int r = 0; r < MR; r++) {
-        const float x = xs[r * kchunk + kk + u * 8];
-        acc[r].x = fmaf(x, wv[u].x, acc[r].x);
-        acc[r].y = fmaf(x, wv[u].y, acc[r].y);
-        acc[r].z = fmaf(x, wv[u].z, acc[r].z);
-        acc[r].w = fmaf(x, wv[u].w, acc[r].w);
-      }
+    for (int u = 0; u < kGemvUnroll; u++) {
+      acc.x = fmaf(xv[u], wv[u].x, acc.x);
+      acc.y = fmaf(xv[u], wv[u].y, acc.y);
+      acc.z = fmaf(xv[u], wv[u].z, acc.z);
+      acc.w = fmaf(xv[u], wv[u].w, acc.w);
+    }
+    p += kGemvUnroll * step;
   }
-  for (; kk < kn; kk += 8) {
-    const float *src = W + (k0 + kk) * ldw + c0;
+  for (; k < k1; k += 8, p += step) {
     float4 wv;
-    if (full) wv = __ldg(reinterpret_cast<const float4 *>(src));
-    else {
-      wv.x = c0 < N ? src[0] : 0.f; wv.y = c0 + 1 < N ? src[1] : 0.f;
-      wv.z = c0 + 2 < N ? src[2] : 0.f; wv.w = c0 + 3 < N ? src[3] : 0.f;
-    }
+    if (vec) wv = __ldg(reinterpret_cast<const float4 *>(p));
+    else wv = make_float4(c0 < N ? p[0] : 0.f, c0 + 1 < N ? p[1] : 0.f, c0 + 2 < N ? p[2] : 0.f, 0.f);
+    const float xv = __ldg(x + k);
+    acc.x = fmaf(xv, wv.x, acc.x);
+    acc.y = fmaf(xv, wv.y, acc.y);
+    acc.z = fmaf(xv, wv.z, acc.z);
+    acc.w = fmaf(xv, wv.w, acc.w);
+  }
+  wsum[w][lane] = acc;
+  __syncthreads();
+  float *tile = reinterpret_cast<float *>(&wsum[0][0]);  // 128 column sums after the warp combine
+  if (w == 0) {
+    float4 v = wsum[0][lane];
 #pragma unroll
-    for (int r = 0; r < MR; r++) {
-      const float x = xs[r * kchunk + kk];
-      acc[r].x = fmaf(x, wv.x, acc[r].x);
-      acc[r].y = fmaf(x, wv.y, acc[r].y);
-      acc[r].z = fmaf(x, wv.z, acc[r].z);
-      acc[r].w = fmaf(x, wv.w, acc[r].w);
+    for (int j = 1; j < 8; j++) {
+      const float4 t = wsum[j][lane];
+      v.x += t.x; v.y += t.y; v.z += t.z; v.w += t.w;
+    }
+    __syncwarp();
+    wsum[0][lane] = v;
+  }
+  // The cluster's CTAs are consecutive K slices of this column tile: rank q
+  // adds columns [q*128/CL, (q+1)*128/CL) over the ranks in order.
+  cg::cluster_group cl = cg::this_cluster();
+  cl.sync();
+  const int CL = int(cl.num_blocks()), q = int(cl.block_rank());
+  const int per = 128 / CL;
+  if (int(threadIdx.x) < per) {
+    const int c = q * per + threadIdx.x;
+    float v = 0.0f;
+    for (int j = 0; j < CL; j++) v += cl.map_shared_rank(tile, j)[c];
+    const int64_t col = int64_t(blockIdx.x) * 128 + c;
+    if (col < N) {
+      if (part) part[int64_t(blockIdx.y / CL) * N + col] = v;
+      else out[col] = apply_epi(epi, v, 0, col);
     }
   }
-  // Combine the 8 warps in warp order (deterministic).
-  for (int ww = 0; ww < 8; ww++) {
-    if (w == ww) {
-#pragma unroll
-      for (int r = 0; r < MR; r++) {
-        red[r][lane * 4 + 0] += acc[r].x;
-        red[r][lane * 4 + 1] += acc[r].y;
-        red[r][lane * 4 + 2] += acc[r].z;
-        red[r][lane * 4 + 3] += acc[r].w;
-      }
-    }
-    __syncthreads();
-  }
-  for (int e = threadIdx.x; e < MR * 128; e += 256) {
-    const int r = e / 128, c = e % 128;
-    const int64_t row = m0 + r, col = int64_t(blockIdx.x) * 128 + c;
-    if (row >= M || col >= N) continue;
-    if (part) part[(int64_t(blockIdx.y) * M + row) * N + col] = red[r][c];
-    else out[row * ldo + col] = apply_epi(epi, red[r][c], row, col);
-  }
+  cl.sync();
 }
 
-__global__ void __launch_bounds__(256) skinny_finish(const float *__restrict__ part, int splits,
+__global__ void __launch_bounds__(256) skinny_finish(const float *__restrict__ part, int groups,
                                                      float *__restrict__ out, int64_t ldo, int64_t M,
                                                      int64_t N, Epi epi) {
   const int64_t j = int64_t(blockIdx.x) * 256 + threadIdx.x;
   if (j >= M * N) return;
   const int64_t row = j / N, col = j % N;
+  // Loads batched 16 at a time (independent, in flight together); the adds
+  // keep group order.
+  const int64_t stride = M * N;
   float s = 0.0f;
-  for (int sp = 0; sp < splits; sp++) s += part[int64_t(sp) * M * N + j];
+  for (int g0 = 0; g0 < groups; g0 += 16) {
+    float v[16];
+#pragma unroll
+    for (int u = 0; u < 16; u++) v[u] = g0 + u < groups ? part[int64_t(g0 + u) * stride + j] : 0.0f;
+#pragma unroll
+    for (int u = 0; u < 16; u++)
+      if (g0 + u < groups) s += v[u];
+  }
   out[row * ldo + col] = apply_epi(epi, s, row, col);
 }
 
 struct SkinnyPlan {
-  int mr, splits;
-  int64_t kchunk;
+  int mr, cpl, groups;  // groups: cluster groups along K (> 1 needs the finish pass)
+  int64_t kchunk;       // K per CTA
 };
+
+int skinny_unroll(int mr) { return mr == 32 ? 4 : 8; }
 
 SkinnyPlan skinny_plan(int64_t M, int64_t N, int64_t K) {
   SkinnyPlan pl;
-  pl.mr = M == 1 ? 1 : (M <= 4 ? 4 : (M <= 8 ? 8 : 16));
-  const int64_t col_tiles = (N + 127) / 128;
-  const int64_t m_tiles = (M + pl.mr - 1) / pl.mr;
-  const int64_t target = int64_t(sm_count()) * 6;
-  int64_t sp = (target + col_tiles * m_tiles - 1) / (col_tiles * m_tiles);
-  const int64_t max_sp = K / 64 > 0 ? K / 64 : 1;
-  if (sp > max_sp) sp = max_sp;
-  if (sp < 1) sp = 1;
-  int64_t kchunk = (K + sp - 1) / sp;
-  kchunk = (kchunk + 31) / 32 * 32;
-  // keep the X tile in shared memory within 64 KB
-  const int64_t max_chunk = (64 * 1024) / (4 * pl.mr);
-  if (kchunk > max_chunk) kchunk = max_chunk / 32 * 32;
+  if (M <= 8) { pl.mr = 8; pl.cpl = 2; }
+  else if (M <= 16) { pl.mr = 16; pl.cpl = 1; }
+  else { pl.mr = 32; pl.cpl = 1; }
+  // Slices of 256 k: few enough CTAs that the per-CTA costs
+  // (X staging, cluster combine) stay small, long enough chains of W loads
+  // per warp to keep HBM busy.
+  const int64_t step = 8 * skinny_unroll(pl.mr);
+  const int64_t target = kSkinnyMaxChunk;
+  int64_t groups = (K + target * kSkinnyCluster - 1) / (target * kSkinnyCluster);
+  if (groups < 1) groups = 1;
+  int64_t kchunk = (K + groups * kSkinnyCluster - 1) / (groups * kSkinnyCluster);
+  kchunk = (kchunk + step - 1) / step * step;
   pl.kchunk = kchunk;
-  pl.splits = int((K + kchunk - 1) / kchunk);
-  if (pl.splits < 1) pl.splits = 1;
+  pl.groups = int((K + kchunk * kSkinnyCluster - 1) / (kchunk * kSkinnyCluster));
+  if (pl.groups < 1) pl.groups = 1;
   return pl;
 }
 
-template <int MR>
+size_t skinny_part_bytes(const SkinnyPlan &pl, int64_t M, int64_t N) {
+  return pl.groups > 1 ? size_t(pl.groups) * M * N * sizeof(float) : 0;
+}
+
+struct GemvPlan {
+  int cluster, groups;  // K slices = cluster * groups; groups > 1 needs the finish pass
+  int64_t kchunk;
+};
+
+// Cluster size for the K slices: 8, or 16 when 8 slices per column tile
+// would leave SMs idle (environment SILCU_GEMV_CLUSTER = 1/2/4/8/16
+// overrides, for tuning).
+int gemv_cluster(int64_t tiles, int64_t K) {
+  static const int forced = [] {
+    const char *e = getenv("SILCU_GEMV_CLUSTER");
+    const int x = e ? atoi(e) : 0;
+    return (x == 1 || x == 2 || x == 4 || x == 8 || x == 16) ? x : 0;
+  }();
+  if (forced) return forced;
+  return (tiles * 8 < sm_count() && K >= 16 * 64) ? 16 : 8;
+}
+
+// One cluster group while the slices stay <= 1024 rows; multiples of 64 rows.
+GemvPlan gemv_plan(int64_t N, int64_t K) {
+  GemvPlan pl;
+  pl.cluster = gemv_cluster((N + 127) / 128, K);
+  int64_t groups = (K + int64_t(pl.cluster) * 1024 - 1) / (int64_t(pl.cluster) * 1024);
+  if (groups < 1) groups = 1;
+  int64_t kchunk = (K + groups * pl.cluster - 1) / (groups * pl.cluster);
+  kchunk = (kchunk + 63) / 64 * 64;
+  pl.kchunk = kchunk;
+  pl.groups = int((K + kchunk * pl.cluster - 1) / (kchunk * pl.cluster));
+  if (pl.groups < 1) pl.groups = 1;
+  return pl;
+}
+
+size_t gemv_part_bytes(const GemvPlan &pl, int64_t N) {
+  return pl.groups > 1 ? size_t(pl.groups) * N * sizeof(float) : 0;
+}
+
+cudaError_t launch_gemv(const GemvPlan &pl, const float *x, const float *W, int64_t ldw, float *out, int64_t N,
+                        int64_t K, float *part, const Epi &epi, cudaStream_t s) {
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (pl.cluster > 8 && dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(uint32_t((N + 127) / 128), uint32_t(pl.groups * pl.cluster));
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 1;
+  at[0].val.clusterDim.y = unsigned(pl.cluster);
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  float *p = pl.groups > 1 ? part : nullptr;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel, x, W, ldw, out, N, K, pl.kchunk, p, epi);
+  if (e != cudaSuccess) return e;
+  if (pl.groups > 1)
+    skinny_finish<<<uint32_t((N + 255) / 256), 256, 0, s>>>(part, pl.groups, out, N, 1, N, epi);
+  return cudaSuccess;
+}
+
+template <int MR, int CPL, int UNROLL>
 void launch_skinny(const SkinnyPlan &pl, const float *X, int64_t ldx, const float *W, int64_t ldw, float *out,
                    int64_t ldo, int64_t M, int64_t N, int64_t K, float *part, const Epi &epi,
                    cudaStream_t s) {
-  dim3 grid(uint32_t((N + 127) / 128), uint32_t(pl.splits), uint32_t((M + MR - 1) / MR));
-  const size_t smem = size_t(MR) * pl.kchunk * sizeof(float);
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(skinny_gemm<MR>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
-    configured = true;
+  constexpr int COLS = 32 * CPL;
+  dim3 grid(uint32_t((N + COLS - 1) / COLS), uint32_t(pl.groups * kSkinnyCluster),
+            uint32_t((M + MR - 1) / MR));
+  const size_t smem = (size_t(9) * MR * COLS + size_t(MR) * pl.kchunk) * sizeof(float);
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaFuncSetAttribute(skinny_gemm<MR, CPL, UNROLL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         int((9 * MR * COLS + MR * kSkinnyMaxChunk) * sizeof(float)));
+    configured[dev] = true;
   }
-  skinny_gemm<MR><<<grid, 256, smem, s>>>(X, ldx, W, ldw, out, ldo, M, N, K, pl.kchunk,
-                                          pl.splits > 1 ? part : nullptr, epi);
-  if (pl.splits > 1) {
+  skinny_gemm<MR, CPL, UNROLL><<<grid, 256, smem, s>>>(X, ldx, W, ldw, out, ldo, M, N, K, pl.kchunk,
+                                                       pl.groups > 1 ? part : nullptr, epi);
+  if (pl.groups > 1) {
     const int64_t total = M * N;
-    skinny_finish<<<uint32_t((total + 255) / 256), 256, 0, s>>>(part, pl.splits, out, ldo, M, N, epi);
+    skinny_finish<<<uint32_t((total + 255) / 256), 256, 0, s>>>(part, pl.groups, out, ldo, M, N, epi);
   }
 }
 
@@ -351,8 +594,9 @@ size_t silcu_sgemm_workspace_bytes(const silcu_gemm_args *a) {
   switch (gemm_path(*a)) {
     case kPathTc: return tc_workspace_bytes(*a);
     case kPathSkinny: {
+      if (a->M == 1) return gemv_part_bytes(gemv_plan(a->N, a->K), a->N);
       SkinnyPlan pl = skinny_plan(a->M, a->N, a->K);
-      return pl.splits > 1 ? size_t(pl.splits) * a->M * a->N * sizeof(float) : 0;
+      return skinny_part_bytes(pl, a->M, a->N);
     }
     default: return 0;
   }
@@ -368,19 +612,27 @@ silcu_status silcu_sgemm_ex(const silcu_gemm_args *ap, void *ws, size_t wsb, sil
   const Epi epi = make_epi(a);
   const int path = gemm_path(a);
   if (path == kPathTc) return tc_run(a, ws, wsb, s);
+  if (path == kPathSkinny && a.M == 1) {
+    const GemvPlan pl = gemv_plan(a.N, a.K);
+    const size_t need = gemv_part_bytes(pl, a.N);
+    if (need && (!ws || wsb < need))
+      return fail(SILCU_WORKSPACE_TOO_SMALL, "sgemm(gemv): workspace %zu < %zu", wsb, need);
+    const cudaError_t e = launch_gemv(pl, a.A, a.B, a.ldb, a.C, a.N, a.K, static_cast<float *>(ws), epi, s);
+    if (e != cudaSuccess) return fail(SILCU_CUDA_ERROR, "sgemm(gemv): %s", cudaGetErrorString(e));
+    return check_launch("sgemm(gemv)", pl.groups > 1 ? 2 : 1);
+  }
   if (path == kPathSkinny) {
     SkinnyPlan pl = skinny_plan(a.M, a.N, a.K);
-    const size_t need = pl.splits > 1 ? size_t(pl.splits) * a.M * a.N * sizeof(float) : 0;
+    const size_t need = skinny_part_bytes(pl, a.M, a.N);
     if (need && (!ws || wsb < need))
       return fail(SILCU_WORKSPACE_TOO_SMALL, "sgemm(skinny): workspace %zu < %zu", wsb, need);
     float *part = static_cast<float *>(ws);
     switch (pl.mr) {
-      case 1: launch_skinny<1>(pl, a.A, a.lda, a.B, a.ldb, a.C, a.ldc, a.M, a.N, a.K, part, epi, s); break;
-      case 4: launch_skinny<4>(pl, a.A, a.lda, a.B, a.ldb, a.C, a.ldc, a.M, a.N, a.K, part, epi, s); break;
-      case 8: launch_skinny<8>(pl, a.A, a.lda, a.B, a.ldb, a.C, a.ldc, a.M, a.N, a.K, part, epi, s); break;
-      default: launch_skinny<16>(pl, a.A, a.lda, a.B, a.ldb, a.C, a.ldc, a.M, a.N, a.K, part, epi, s); break;
+      case 8: launch_skinny<8, 2, 8>(pl, a.A, a.lda, a.B, a.ldb, a.C, a.ldc, a.M, a.N, a.K, part, epi, s); break;
+      case 16: launch_skinny<16, 1, 8>(pl, a.A, a.lda, a.B, a.ldb, a.C, a.ldc, a.M, a.N, a.K, part, epi, s); break;
+      default: launch_skinny<32, 1, 4>(pl, a.A, a.lda, a.B, a.ldb, a.C, a.ldc, a.M, a.N, a.K, part, epi, s); break;
     }
-    return check_launch("sgemm(skinny)", pl.splits > 1 ? 2 : 1);
+    return check_launch("sgemm(skinny)", pl.groups > 1 ? 2 : 1);
   }
   const int64_t bin = a.batch_inner > 1 ? a.batch_inner : 1;
   if (a.batch * bin > 65535) return fail(SILCU_UNSUPPORTED, "sgemm(ffma): batch > 65535");
@@ -442,8 +694,7 @@ silcu_status silcu_sgemm_bias_sigmoid(const float *A, const float *B, float *C, 
 }
 
 size_t silcu_sgemv_workspace_bytes(uint32_t N, uint32_t K) {
-  SkinnyPlan pl = skinny_plan(1, N, K);
-  return pl.splits > 1 ? size_t(pl.splits) * N * sizeof(float) : 0;
+  return gemv_part_bytes(gemv_plan(N, K), N);
 }
 
 silcu_status silcu_sgemv(const float *x, const float *W, float *y, const float *bias, uint32_t N, uint32_t K,

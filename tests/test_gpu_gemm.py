@@ -147,3 +147,19 @@ def test_split_operands_and_split_output(cuda):
     got2 = host(gpu.gemm((dev(ah), dev(al)), (dev(b_h), dev(b_l)), M=M, N=N, K=K))
     np.testing.assert_array_equal(got2, ref)
     assert_dot_close(ref.reshape(M, N), O.sgemm(a, bt, tb=True), K, what="split")
+
+
+@pytest.mark.parametrize("M", [1, 2, 8, 9, 33, 64])
+@pytest.mark.parametrize("N,K", [(1001, 777), (96, 20000), (4100, 64)])
+def test_skinny_shapes_with_epilogue(cuda, M, N, K):
+    """The M <= 64 streaming path: ragged N (partial column tiles), K split
+    over CTAs (partials combined in a fixed order), bias + relu epilogue."""
+    rng = np.random.default_rng(M * 31 + N + K)
+    a = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    b = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    bias = rng.uniform(-1, 1, N).astype(np.float32)
+    got = host(gpu.gemm(dev(a), dev(b), M=M, N=N, K=K, bias=dev(bias), act="relu")).reshape(M, N)
+    ref = np.maximum(O.binary("add", O.sgemm(a, b).ravel(), bias).reshape(M, N), 0)
+    assert_dot_close(got, ref, K, what=f"skinny {M}x{N}x{K}")
+    again = host(gpu.gemm(dev(a), dev(b), M=M, N=N, K=K, bias=dev(bias), act="relu")).reshape(M, N)
+    np.testing.assert_array_equal(got, again)
