@@ -3,9 +3,11 @@
 //   ffma_gemm   128x128x8 tiles, 256 threads, 8x8 outputs per thread, fp32
 //               FFMA.  Handles every stride/transpose/batch/tail case and is
 //               the accuracy reference for the tensor-core path.
-//   skinny_gemm M <= 64 (GEMV at M = 1): each thread streams 2-4 columns of
-//               W with K split across warps and CTAs, so W is read from HBM
-//               once; partials are combined in a fixed order.
+//   gemv_kernel  M = 1: float4 streams of W, K slices combined in a thread
+//                block cluster through distributed shared memory (HBM-bound).
+//   small_m_gemm 2 <= M <= 64: 4x4 register micro-tiles over a cp.async ring,
+//                split K combined in a cluster the same way.
+//   Both sum in a fixed order, so results are deterministic.
 //   tensor-core 3xTF32 tcgen05 path lives in tc_gemm.cu.
 #include <stdlib.h>
 #include <string.h>
@@ -147,160 +149,145 @@ __global__ void __launch_bounds__(256) ffma_gemm(const FfmaArgs p) {
   }
 }
 
-// ------------------------------------------------------- skinny GEMM / GEMV
-// HBM-bound: W is streamed once.  A CTA (8 warps) owns a tile of 32*CPL
-// columns (lane l holds CPL consecutive columns), MR rows of X and one K
-// slice; its warps take the slice's k round-robin with UNROLL W loads in
-// flight per thread, the first batch issued before X's slice is staged
-// (transposed, [k][m], so the MR values of one k are broadcast loads).  The
-// K slices of a tile run as one 8-CTA cluster and are combined through
-// distributed shared memory in rank order; with more than 8 slices per tile,
-// G cluster groups write partials that skinny_finish adds in group order.
-// Every sum has a fixed order, so results are deterministic.
-constexpr int kSkinnyCluster = 8;
-constexpr int kSkinnyMaxChunk = 256;  // K per CTA at most
+// ------------------------------------------------------- small M / GEMV
+// Small M (2..64): register-blocked FFMA with split K.  A CTA computes an
+// MT x 64 tile of C over one K slice with 4*MT threads, each a 4 x 4
+// micro-tile (64 FMAs per eight 128-bit shared loads).  K runs in stages of
+// 32 through a kSmStages-deep cp.async ring: the W stage (32 x 64) and the X
+// stage (MT x 32, rows padded to 36 floats) are 16-byte copies, zero-filled
+// past N, past M and past the slice.  The slices of a tile run as one cluster
+// and combine in rank order through distributed shared memory; with more
+// slices than the cluster holds, each cluster writes a partial that
+// partial_finish adds in order.
+constexpr int kSmCols = 64;
+constexpr int kSmStage = 32;
+constexpr int kSmStages = 4;
+constexpr int kSmXPitch = kSmStage + 4;
 
-template <int MR, int CPL, int UNROLL>
-__global__ void __cluster_dims__(1, kSkinnyCluster, 1) __launch_bounds__(256, MR <= 8 ? 4 : 1)
-    skinny_gemm(const float *__restrict__ X, int64_t ldx, const float *__restrict__ W, int64_t ldw,
-                float *__restrict__ out, int64_t ldo, int64_t M, int64_t N, int64_t K, int64_t kchunk,
-                float *__restrict__ part, Epi epi) {
+template <int MT>
+constexpr size_t small_m_smem() {
+  return size_t(kSmStages) * (kSmStage * kSmCols + MT * kSmXPitch) * sizeof(float);
+}
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, int bytes) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void cp_async4(void *dst, const void *src, int bytes) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(d), "l"(src), "r"(bytes) : "memory");
+}
+
+template <int MT>
+__global__ void __launch_bounds__(4 * MT) small_m_gemm(const float *__restrict__ X, int64_t ldx,
+                                                       const float *__restrict__ W, int64_t ldw,
+                                                       float *__restrict__ out, int64_t ldo, int64_t M,
+                                                       int64_t N, int64_t K, int64_t kchunk,
+                                                       float *__restrict__ part, Epi epi) {
   namespace cg = cooperative_groups;
-  constexpr int COLS = 32 * CPL, E = MR * COLS;
-  extern __shared__ float4 smem4[];
-  float *wred = reinterpret_cast<float *>(smem4);  // [8][E] per-warp sums
-  float *red = wred + 8 * E;                       // [E] CTA sum (read by the cluster)
-  float *xs = red + E;                             // [kchunk][MR]
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const int64_t col0 = int64_t(blockIdx.x) * COLS;
-  const int64_t c0 = col0 + lane * CPL;
+  constexpr int T = 4 * MT;
+  extern __shared__ float4 sm_small[];
+  float *wbase = reinterpret_cast<float *>(sm_small);        // [kSmStages][32][64]
+  float *xbase = wbase + kSmStages * kSmStage * kSmCols;      // [kSmStages][MT][36]
+  const int tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
+  const int64_t col0 = int64_t(blockIdx.x) * kSmCols, m0 = int64_t(blockIdx.z) * MT;
   const int64_t k0 = int64_t(blockIdx.y) * kchunk;
   const int64_t kend = k0 + kchunk < K ? k0 + kchunk : K;
-  const int kn = kend > k0 ? int(kend - k0) : 0;
-  const int64_t m0 = int64_t(blockIdx.z) * MR;
-  const bool full = c0 + CPL <= N && ((reinterpret_cast<uintptr_t>(W + c0) & (4 * CPL - 1)) == 0);
-  auto loadw = [&](int kk, float (&wv)[CPL]) {
-    if (kk >= kn) {
-#pragma unroll
-      for (int c = 0; c < CPL; c++) wv[c] = 0.0f;
-      return;
-    }
-    const float *src = W + (k0 + kk) * ldw + c0;
-    if (full) {
-      if constexpr (CPL == 4) {
-        const float4 f = __ldg(reinterpret_cast<const float4 *>(src));
-        wv[0] = f.x; wv[1] = f.y; wv[2] = f.z; wv[3] = f.w;
-      } else if constexpr (CPL == 2) {
-        const float2 f = __ldg(reinterpret_cast<const float2 *>(src));
-        wv[0] = f.x; wv[1] = f.y;
-      } else {
-        wv[0] = __ldg(src);
+  const int nst = kend > k0 ? int((kend - k0 + kSmStage - 1) / kSmStage) : 0;
+  const bool xvec = (ldx % 4) == 0 && (reinterpret_cast<uintptr_t>(X) & 15) == 0;
+
+  auto load_stage = [&](int st) {
+    const int buf = st % kSmStages;
+    const int64_t kb = k0 + int64_t(st) * kSmStage;
+    float *wsb = wbase + buf * kSmStage * kSmCols;
+    for (int i = tid; i < kSmStage * (kSmCols / 4); i += T) {
+      const int kk = i / (kSmCols / 4), q = i % (kSmCols / 4);
+      const int64_t k = kb + kk, col = col0 + 4 * q;
+      int bytes = 0;
+      if (k < kend) {
+        const int64_t left = N - col;
+        bytes = left >= 4 ? 16 : (left > 0 ? int(left) * 4 : 0);
       }
-    } else {
+      cp_async16(wsb + kk * kSmCols + 4 * q, bytes ? W + k * ldw + col : W, bytes);
+    }
+    float *xsb = xbase + buf * MT * kSmXPitch;
+    for (int i = tid; i < MT * (kSmStage / 4); i += T) {
+      const int r = i / (kSmStage / 4), q = i % (kSmStage / 4);
+      const int64_t row = m0 + r, k = kb + 4 * q;
+      const int64_t left = row < M ? kend - k : 0;
+      const float *src = X + row * ldx + k;
+      float *dst = xsb + r * kSmXPitch + 4 * q;
+      if (xvec) {
+        const int bytes = left >= 4 ? 16 : (left > 0 ? int(left) * 4 : 0);
+        cp_async16(dst, bytes ? src : X, bytes);
+      } else {
 #pragma unroll
-      for (int c = 0; c < CPL; c++) wv[c] = c0 + c < N ? src[c] : 0.0f;
+        for (int u = 0; u < 4; u++) cp_async4(dst + u, u < left ? src + u : X, u < left ? 4 : 0);
+      }
     }
   };
-  float acc[MR][CPL];
+
+  float acc[4][4];
 #pragma unroll
-  for (int r = 0; r < MR; r++)
+  for (int i = 0; i < 4; i++)
 #pragma unroll
-    for (int c = 0; c < CPL; c++) acc[r][c] = 0.0f;
-  auto fma_row = [&](int kk, const float (&wv)[CPL]) {
-    const float *xr = xs + kk * MR;
-    constexpr int V = MR >= 4 ? 4 : 1;
+    for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
 #pragma unroll
-    for (int r = 0; r < MR; r += V) {
-      float xv[4];
-      if constexpr (V == 4) {
-        const float4 f = *reinterpret_cast<const float4 *>(xr + r);
-        xv[0] = f.x; xv[1] = f.y; xv[2] = f.z; xv[3] = f.w;
-      } else {
-        xv[0] = xr[r];
+  for (int st = 0; st < kSmStages - 1; st++) {
+    if (st < nst) load_stage(st);
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+  }
+  for (int st = 0; st < nst; st++) {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(kSmStages - 2) : "memory");
+    __syncthreads();  // stage st landed for every thread; stage st-1's buffer is free
+    if (st + kSmStages - 1 < nst) load_stage(st + kSmStages - 1);
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    const int buf = st % kSmStages;
+    const float *wsb = wbase + buf * kSmStage * kSmCols;
+    const float *xsb = xbase + buf * MT * kSmXPitch;
+#pragma unroll
+    for (int k4 = 0; k4 < kSmStage / 4; k4++) {
+      float a[4][4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const float4 f = *reinterpret_cast<const float4 *>(xsb + (4 * ty + i) * kSmXPitch + 4 * k4);
+        a[i][0] = f.x; a[i][1] = f.y; a[i][2] = f.z; a[i][3] = f.w;
       }
 #pragma unroll
-      for (int q = 0; q < V; q++)
+      for (int u = 0; u < 4; u++) {
+        const float4 b = *reinterpret_cast<const float4 *>(wsb + (4 * k4 + u) * kSmCols + 4 * tx);
+        const float bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-        for (int c = 0; c < CPL; c++) acc[r + q][c] = fmaf(xv[q], wv[c], acc[r + q][c]);
-    }
-  };
-  // First W batch in flight while X's slice is staged.
-  float wv[UNROLL][CPL];
+        for (int i = 0; i < 4; i++)
 #pragma unroll
-  for (int u = 0; u < UNROLL; u++) loadw(w + 8 * u, wv[u]);
-  // X slice: thread e loads 4 consecutive k of row e % MR (16-byte loads when
-  // aligned), XB loads in flight per thread; the [k][m] stores of a warp hit
-  // consecutive rows, so they are free of bank conflicts.
-  {
-    constexpr int XB = 8;
-    const int k4n = int(kchunk) / 4;  // the whole slice, zero past kn
-    const bool xvec = (ldx % 4) == 0 && (reinterpret_cast<uintptr_t>(X) & 15) == 0;
-    for (int base = threadIdx.x; base < MR * k4n; base += 256 * XB) {
-      float v[XB][4];
-#pragma unroll
-      for (int u = 0; u < XB; u++) {
-        const int e = base + u * 256, r = e % MR, kk = (e / MR) * 4;
-        const float *src = X + (m0 + r) * ldx + k0 + kk;
-        if (e < MR * k4n && m0 + r < M) {
-          if (xvec && kk + 4 <= kn) {
-            const float4 f = __ldg(reinterpret_cast<const float4 *>(src));
-            v[u][0] = f.x; v[u][1] = f.y; v[u][2] = f.z; v[u][3] = f.w;
-          } else {
-#pragma unroll
-            for (int i = 0; i < 4; i++) v[u][i] = kk + i < kn ? src[i] : 0.0f;
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 4; i++) v[u][i] = 0.0f;
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < XB; u++) {
-        const int e = base + u * 256, r = e % MR, kk = (e / MR) * 4;
-        if (e < MR * k4n)
-#pragma unroll
-          for (int i = 0; i < 4; i++) xs[(kk + i) * MR + r] = v[u][i];
+          for (int j = 0; j < 4; j++) acc[i][j] = fmaf(a[i][u], bv[j], acc[i][j]);
       }
     }
   }
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
   __syncthreads();
-  // kchunk is a multiple of 8 * UNROLL and X's slice is zero past kn, so the
-  // loop needs no guards (W loads past kn return 0).
-  for (int kk = w; kk < kchunk; kk += 8 * UNROLL) {
-    if (kk > w) {
+  // CTA tile into shared memory (the ring is free), then the cluster combine.
+  float *red = wbase;  // MT x 64 <= kSmStages x 32 x 64
 #pragma unroll
-      for (int u = 0; u < UNROLL; u++) loadw(kk + 8 * u, wv[u]);
-    }
-#pragma unroll
-    for (int u = 0; u < UNROLL; u++) fma_row(kk + 8 * u, wv[u]);
-  }
-#pragma unroll
-  for (int r = 0; r < MR; r++)
-#pragma unroll
-    for (int c = 0; c < CPL; c++) wred[w * E + r * COLS + lane * CPL + c] = acc[r][c];
-  __syncthreads();
-  for (int e = threadIdx.x; e < E; e += 256) {
-    float v = wred[e];
-#pragma unroll
-    for (int ww = 1; ww < 8; ww++) v += wred[ww * E + e];
-    red[e] = v;
-  }
+  for (int i = 0; i < 4; i++)
+    *reinterpret_cast<float4 *>(&red[(4 * ty + i) * kSmCols + 4 * tx]) =
+        make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
   cg::cluster_group cl = cg::this_cluster();
   cl.sync();
-  // Rank q of the cluster finishes elements [q*E/8, (q+1)*E/8) of the tile.
-  const int q = int(cl.block_rank());
-  const int64_t g = blockIdx.y / kSkinnyCluster;
-  for (int e = q * (E / kSkinnyCluster) + threadIdx.x; e < (q + 1) * (E / kSkinnyCluster); e += 256) {
+  const int CL = int(cl.num_blocks()), q = int(cl.block_rank());
+  constexpr int E = MT * kSmCols;
+  const int per = E / CL;
+  const int64_t g = blockIdx.y / CL;
+  for (int e = q * per + tid; e < (q + 1) * per; e += T) {
     float v = 0.0f;
-#pragma unroll
-    for (int j = 0; j < kSkinnyCluster; j++) v += cl.map_shared_rank(red, j)[e];
-    const int r = e / COLS, c = e % COLS;
-    const int64_t row = m0 + r, col = col0 + c;
+    for (int j = 0; j < CL; j++) v += cl.map_shared_rank(red, j)[e];
+    const int64_t row = m0 + e / kSmCols, col = col0 + e % kSmCols;
     if (row >= M || col >= N) continue;
     if (part) part[(g * M + row) * N + col] = v;
     else out[row * ldo + col] = apply_epi(epi, v, row, col);
   }
-  cl.sync();  // peers' shared memory stays valid until every rank has read it
+  cl.sync();
 }
 
 // GEMV (M = 1): a CTA owns 128 columns (lane l holds 4, float4 loads) and a
@@ -309,7 +296,7 @@ __global__ void __cluster_dims__(1, kSkinnyCluster, 1) __launch_bounds__(256, MR
 // through the read-only cache (one broadcast per warp and row).  The 8 warps
 // combine in warp order in shared memory, then the CL consecutive slices of a
 // cluster combine in rank order through distributed shared memory; with more
-// than CL slices, each cluster writes a partial that skinny_finish adds in
+// than CL slices, each cluster writes a partial that partial_finish adds in
 // order.
 constexpr int kGemvUnroll = 8;
 
@@ -393,7 +380,7 @@ __global__ void __launch_bounds__(256, 4) gemv_kernel(const float *__restrict__ 
   cl.sync();
 }
 
-__global__ void __launch_bounds__(256) skinny_finish(const float *__restrict__ part, int groups,
+__global__ void __launch_bounds__(256) partial_finish(const float *__restrict__ part, int groups,
                                                      float *__restrict__ out, int64_t ldo, int64_t M,
                                                      int64_t N, Epi epi) {
   const int64_t j = int64_t(blockIdx.x) * 256 + threadIdx.x;
@@ -414,35 +401,78 @@ __global__ void __launch_bounds__(256) skinny_finish(const float *__restrict__ p
   out[row * ldo + col] = apply_epi(epi, s, row, col);
 }
 
-struct SkinnyPlan {
-  int mr, cpl, groups;  // groups: cluster groups along K (> 1 needs the finish pass)
-  int64_t kchunk;       // K per CTA
+struct SmallMPlan {
+  int mt, cluster, groups;  // K slices = cluster * groups; groups > 1 needs the finish pass
+  int64_t kchunk;
 };
 
-int skinny_unroll(int mr) { return mr == 32 ? 4 : 8; }
+int env_int(const char *name, int lo, int hi, int dflt) {
+  const char *e = getenv(name);
+  const int x = e ? atoi(e) : dflt;
+  return x >= lo && x <= hi ? x : dflt;
+}
 
-SkinnyPlan skinny_plan(int64_t M, int64_t N, int64_t K) {
-  SkinnyPlan pl;
-  if (M <= 8) { pl.mr = 8; pl.cpl = 2; }
-  else if (M <= 16) { pl.mr = 16; pl.cpl = 1; }
-  else { pl.mr = 32; pl.cpl = 1; }
-  // Slices of 256 k: few enough CTAs that the per-CTA costs
-  // (X staging, cluster combine) stay small, long enough chains of W loads
-  // per warp to keep HBM busy.
-  const int64_t step = 8 * skinny_unroll(pl.mr);
-  const int64_t target = kSkinnyMaxChunk;
-  int64_t groups = (K + target * kSkinnyCluster - 1) / (target * kSkinnyCluster);
+// Cluster of 8 slices (4 for 64-row tiles, whose CTAs are 256 threads), 16
+// when 8 per tile would leave SMs idle; slices of at most 1024 k (more become
+// cluster groups), multiples of the 32-k stage.  SILCU_SMALLM_CLUSTER and
+// SILCU_SMALLM_GROUPS override, for tuning.
+SmallMPlan small_m_plan(int64_t M, int64_t N, int64_t K) {
+  SmallMPlan pl;
+  pl.mt = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
+  const int64_t tiles = (N + kSmCols - 1) / kSmCols * ((M + pl.mt - 1) / pl.mt);
+  static const int forced_cl = env_int("SILCU_SMALLM_CLUSTER", 1, 16, 0);
+  static const int min_groups = env_int("SILCU_SMALLM_GROUPS", 1, 64, 1);
+  if (forced_cl) pl.cluster = forced_cl;
+  else if (tiles * 8 < int64_t(sm_count()) && K >= 16 * 64) pl.cluster = 16;
+  else pl.cluster = pl.mt == 64 ? 4 : 8;
+  int64_t groups = (K + int64_t(pl.cluster) * 1024 - 1) / (int64_t(pl.cluster) * 1024);
+  if (groups < min_groups) groups = min_groups;
   if (groups < 1) groups = 1;
-  int64_t kchunk = (K + groups * kSkinnyCluster - 1) / (groups * kSkinnyCluster);
-  kchunk = (kchunk + step - 1) / step * step;
+  int64_t kchunk = (K + groups * pl.cluster - 1) / (groups * pl.cluster);
+  kchunk = (kchunk + kSmStage - 1) / kSmStage * kSmStage;
   pl.kchunk = kchunk;
-  pl.groups = int((K + kchunk * kSkinnyCluster - 1) / (kchunk * kSkinnyCluster));
+  pl.groups = int((K + kchunk * pl.cluster - 1) / (kchunk * pl.cluster));
   if (pl.groups < 1) pl.groups = 1;
   return pl;
 }
 
-size_t skinny_part_bytes(const SkinnyPlan &pl, int64_t M, int64_t N) {
+size_t small_m_part_bytes(const SmallMPlan &pl, int64_t M, int64_t N) {
   return pl.groups > 1 ? size_t(pl.groups) * M * N * sizeof(float) : 0;
+}
+
+template <int MT>
+cudaError_t launch_small_m(const SmallMPlan &pl, const float *X, int64_t ldx, const float *W, int64_t ldw,
+                           float *out, int64_t ldo, int64_t M, int64_t N, int64_t K, float *part,
+                           const Epi &epi, cudaStream_t s) {
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaFuncSetAttribute(small_m_gemm<MT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    cudaFuncSetAttribute(small_m_gemm<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(small_m_smem<MT>()));
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(uint32_t((N + kSmCols - 1) / kSmCols), uint32_t(pl.groups * pl.cluster),
+                     uint32_t((M + MT - 1) / MT));
+  cfg.blockDim = dim3(4 * MT);
+  cfg.dynamicSmemBytes = small_m_smem<MT>();
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 1;
+  at[0].val.clusterDim.y = unsigned(pl.cluster);
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  float *p = pl.groups > 1 ? part : nullptr;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, small_m_gemm<MT>, X, ldx, W, ldw, out, ldo, M, N, K, pl.kchunk, p, epi);
+  if (e != cudaSuccess) return e;
+  if (pl.groups > 1) {
+    const int64_t total = M * N;
+    partial_finish<<<uint32_t((total + 255) / 256), 256, 0, s>>>(part, pl.groups, out, ldo, M, N, epi);
+  }
+  return cudaSuccess;
 }
 
 struct GemvPlan {
@@ -505,32 +535,8 @@ cudaError_t launch_gemv(const GemvPlan &pl, const float *x, const float *W, int6
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel, x, W, ldw, out, N, K, pl.kchunk, p, epi);
   if (e != cudaSuccess) return e;
   if (pl.groups > 1)
-    skinny_finish<<<uint32_t((N + 255) / 256), 256, 0, s>>>(part, pl.groups, out, N, 1, N, epi);
+    partial_finish<<<uint32_t((N + 255) / 256), 256, 0, s>>>(part, pl.groups, out, N, 1, N, epi);
   return cudaSuccess;
-}
-
-template <int MR, int CPL, int UNROLL>
-void launch_skinny(const SkinnyPlan &pl, const float *X, int64_t ldx, const float *W, int64_t ldw, float *out,
-                   int64_t ldo, int64_t M, int64_t N, int64_t K, float *part, const Epi &epi,
-                   cudaStream_t s) {
-  constexpr int COLS = 32 * CPL;
-  dim3 grid(uint32_t((N + COLS - 1) / COLS), uint32_t(pl.groups * kSkinnyCluster),
-            uint32_t((M + MR - 1) / MR));
-  const size_t smem = (size_t(9) * MR * COLS + size_t(MR) * pl.kchunk) * sizeof(float);
-  static bool configured[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaFuncSetAttribute(skinny_gemm<MR, CPL, UNROLL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         int((9 * MR * COLS + MR * kSkinnyMaxChunk) * sizeof(float)));
-    configured[dev] = true;
-  }
-  skinny_gemm<MR, CPL, UNROLL><<<grid, 256, smem, s>>>(X, ldx, W, ldw, out, ldo, M, N, K, pl.kchunk,
-                                                       pl.groups > 1 ? part : nullptr, epi);
-  if (pl.groups > 1) {
-    const int64_t total = M * N;
-    skinny_finish<<<uint32_t((total + 255) / 256), 256, 0, s>>>(part, pl.groups, out, ldo, M, N, epi);
-  }
 }
 
 bool skinny_eligible(const silcu_gemm_args &a) {
@@ -595,8 +601,7 @@ size_t silcu_sgemm_workspace_bytes(const silcu_gemm_args *a) {
     case kPathTc: return tc_workspace_bytes(*a);
     case kPathSkinny: {
       if (a->M == 1) return gemv_part_bytes(gemv_plan(a->N, a->K), a->N);
-      SkinnyPlan pl = skinny_plan(a->M, a->N, a->K);
-      return skinny_part_bytes(pl, a->M, a->N);
+      return small_m_part_bytes(small_m_plan(a->M, a->N, a->K), a->M, a->N);
     }
     default: return 0;
   }
@@ -622,17 +627,19 @@ silcu_status silcu_sgemm_ex(const silcu_gemm_args *ap, void *ws, size_t wsb, sil
     return check_launch("sgemm(gemv)", pl.groups > 1 ? 2 : 1);
   }
   if (path == kPathSkinny) {
-    SkinnyPlan pl = skinny_plan(a.M, a.N, a.K);
-    const size_t need = skinny_part_bytes(pl, a.M, a.N);
+    const SmallMPlan pl = small_m_plan(a.M, a.N, a.K);
+    const size_t need = small_m_part_bytes(pl, a.M, a.N);
     if (need && (!ws || wsb < need))
-      return fail(SILCU_WORKSPACE_TOO_SMALL, "sgemm(skinny): workspace %zu < %zu", wsb, need);
+      return fail(SILCU_WORKSPACE_TOO_SMALL, "sgemm(small M): workspace %zu < %zu", wsb, need);
     float *part = static_cast<float *>(ws);
-    switch (pl.mr) {
-      case 8: launch_skinny<8, 2, 8>(pl, a.A, a.lda, a.B, a.ldb, a.C, a.ldc, a.M, a.N, a.K, part, epi, s); break;
-      case 16: launch_skinny<16, 1, 8>(pl, a.A, a.lda, a.B, a.ldb, a.C, a.ldc, a.M, a.N, a.K, part, epi, s); break;
-      default: launch_skinny<32, 1, 4>(pl, a.A, a.lda, a.B, a.ldb, a.C, a.ldc, a.M, a.N, a.K, part, epi, s); break;
+    cudaError_t e;
+    switch (pl.mt) {
+      case 16: e = launch_small_m<16>(pl, a.A, a.lda, a.B, a.ldb, a.C, a.ldc, a.M, a.N, a.K, part, epi, s); break;
+      case 32: e = launch_small_m<32>(pl, a.A, a.lda, a.B, a.ldb, a.C, a.ldc, a.M, a.N, a.K, part, epi, s); break;
+      default: e = launch_small_m<64>(pl, a.A, a.lda, a.B, a.ldb, a.C, a.ldc, a.M, a.N, a.K, part, epi, s); break;
     }
-    return check_launch("sgemm(skinny)", pl.groups > 1 ? 2 : 1);
+    if (e != cudaSuccess) return fail(SILCU_CUDA_ERROR, "sgemm(small M): %s", cudaGetErrorString(e));
+    return check_launch("sgemm(small M)", pl.groups > 1 ? 2 : 1);
   }
   const int64_t bin = a.batch_inner > 1 ? a.batch_inner : 1;
   if (a.batch * bin > 65535) return fail(SILCU_UNSUPPORTED, "sgemm(ffma): batch > 65535");
