@@ -15,7 +15,8 @@
 //              buffer, then O_j = P_{j-1} V_{j-1}, so S_{j+1} overlaps the
 //              softmax of block j
 //   warps 2-9  thread = query row (two warps per row quarter, each with half
-//              of the keys and of the output columns): scores from TMEM, running max / sum,
+//              of the keys and of the output columns): scores from TMEM, running max / sum
+//              (exponentials on the hardware ex2 unit),
 //              P_j split into hi/lo into TMEM (the A operand of the P.V
 //              MMA), O accumulated in registers with
 //              round-to-nearest adds and rescaled as the max moves.
@@ -89,6 +90,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
+// e^x for x <= 0 as 2^(x log2 e) on the hardware base-2 exponential
+// (ex2.approx: relative error about 2^-22; with the rounding of x log2 e the
+// result is within ~1.5e-6 relative for x >= -30, and exactly 0 at -inf).
+constexpr float kLog2e = 1.44269504088896341f;
+__device__ __forceinline__ float exp_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(__fmul_rn(x, kLog2e)));
+  return y;
+}
+
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_constant__ AttnParams p) {
@@ -249,21 +260,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kSEmpty + s));
       float mj = __int_as_float(0xff800000);
+      const bool tail = (j + 1) * KB > p.Sk;
 #pragma unroll
       for (int i = 0; i < HK; i++) {
         float x = __fmul_rn(sc[i], p.scale);           // the reference's `* scale` node
-        if (j * KB + HK * hh + i >= p.Sk) x = __int_as_float(0xff800000);
+        if (tail && j * KB + HK * hh + i >= p.Sk) x = __int_as_float(0xff800000);
         sc[i] = x;
         mj = fmaxf(mj, x);
       }
       xmax[hh * QT + r] = mj;
       asm volatile("bar.sync 1, 256;" ::: "memory");
       const float m_new = fmaxf(m, fmaxf(xmax[r], xmax[QT + r]));
-      const float corr = (m == m_new) ? 1.0f : expf(__fsub_rn(m, m_new));
+      const float corr = (m == m_new) ? 1.0f : exp_ex2(__fsub_rn(m, m_new));
       float ps = 0.0f;
 #pragma unroll
       for (int i = 0; i < HK; i++) {
-        const float e = expf(__fsub_rn(sc[i], m_new));
+        const float e = exp_ex2(__fsub_rn(sc[i], m_new));
         sc[i] = e;
         ps += e;
       }
@@ -278,11 +290,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
       }
       {
         uint32_t hv[32], lv[32];
+        // P >= 0: round-to-nearest-away to tf32 is "add half a tf32 ulp,
+        // clear the 13 low bits" (integer pipe, not the conversion unit).
 #pragma unroll
         for (int i = 0; i < HK; i++) {
-          const float hx = tf32_rna(sc[i]);
-          hv[i] = __float_as_uint(hx);
-          lv[i] = __float_as_uint(__fsub_rn(sc[i], hx));
+          const uint32_t hb = (__float_as_uint(sc[i]) + 0x1000u) & 0xFFFFE000u;
+          hv[i] = hb;
+          lv[i] = __float_as_uint(__fsub_rn(sc[i], __uint_as_float(hb)));
         }
         const uint32_t pcol = lane_base + COL_P + 128 * s + HK * hh;
         tmem_st32(pcol, hv);

@@ -85,6 +85,7 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, uint32_t sr
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -106,6 +107,18 @@ __device__ __forceinline__ void tc_fence_after() {
 // Shared-memory matrix descriptor, K-major operand with 128-byte swizzle:
 // 8-row x 128-byte swizzle atoms stacked along M/N every 1024 bytes (SBO);
 // LBO is unused for this layout (encoded as 1); version 1 (sm_100).
+// K-major operand, 64-byte swizzle: rows of 16 fp32 (64 B), 8-row groups
+// 512 B apart (the layout a SWIZZLE_64B TMA box of 16 fp32 writes).
+__device__ __forceinline__ uint64_t make_desc_sw64(uint32_t addr) {
+  uint64_t d = 0;
+  d |= uint64_t((addr & 0x3FFFFu) >> 4);
+  d |= uint64_t(1) << 16;
+  d |= uint64_t(512 >> 4) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(4) << 61;
+  return d;
+}
+
 __device__ __forceinline__ uint64_t make_desc(uint32_t addr) {
   uint64_t d = 0;
   d |= uint64_t((addr & 0x3FFFFu) >> 4);
@@ -171,7 +184,8 @@ inline EncodeTiledFn encode_fn() {
 // s_out}, boxes {box0, box1, 1, 1}, 128-byte swizzle.  Strides of extent-1
 // dimensions are replaced by a valid dummy.
 inline bool make_map4(CUtensorMap *m, const float *base, int64_t inner, int64_t rows, int64_t ld, int64_t bin,
-               int64_t s_in, int64_t bout, int64_t s_out, int box0, int box1) {
+               int64_t s_in, int64_t bout, int64_t s_out, int box0, int box1,
+               CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const int64_t span = ld * rows;
@@ -182,7 +196,7 @@ inline bool make_map4(CUtensorMap *m, const float *base, int64_t inner, int64_t 
   cuuint32_t box[4] = {cuuint32_t(box0), cuuint32_t(box1), 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float *>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }

@@ -10,8 +10,9 @@
 //               e.g. written by the producing kernel); otherwise a pre-pass
 //               (pack_split / split_contig) writes hi/lo copies, K-major, K
 //               padded to a multiple of 32;
-//   warp 0      TMA producer: 4 boxes of 128 rows x 32 fp32 (128 B, 128-byte
-//               swizzle) per K block into a 3-stage shared-memory ring;
+//   warp 0      TMA producer: 4 boxes (A, B x hi, lo) of 16 fp32 per row
+//               (64 B, 64-byte swizzle) per K block into a 4- to 8-stage
+//               shared-memory ring;
 //   warp 1      allocates all 512 TMEM columns (4 accumulator buffers of 128),
 //               one thread issues tcgen05.mma.kind::tf32 (M=128, N=128, K=8)
 //               x 3 per K step and tcgen05.commit to release ring slots and to
@@ -36,12 +37,17 @@ namespace silcu {
 namespace {
 using namespace tc;
 
-constexpr int BM = 128, BK = 32;
+constexpr int BM = 128;
+constexpr int BK = 16;    // K per ring stage: one 64-byte swizzle row of fp32
+constexpr int KPAD = 32;  // K padding of the split copies written by the pre-pass
 
-// Per-variant constants: BN = 64 (4-stage ring, 8 TMEM chunk buffers, 4
-// epilogue warps of 64 columns), BN = 128 (3 stages, 4 buffers, 4 warps) or
-// BN = 256 (2 stages, 2 buffers, 8 epilogue warps of 128 columns).  The wider tile halves the shared-memory
-// operand traffic per FLOP of A, which bounds the 128-wide variant.
+// Per-variant constants: BN = 64 (8-stage ring, 8 TMEM chunk buffers, 4
+// epilogue warps of 64 columns), BN = 128 (6 stages, 4 buffers, 4 warps) or
+// BN = 256 (4 stages, 2 buffers, 8 epilogue warps of 128 columns).  The wider
+// tile halves the shared-memory operand traffic per FLOP of A.  Stages of 16
+// k keep several TMA fills in flight while the MMAs consume one: a stage of
+// 32 k at BN = 256 (96 KB) left room for only two, and the fill latency
+// showed up as idle tensor cycles.
 template <int BN_>
 struct Cfg {
   static constexpr int BN = BN_;
@@ -53,7 +59,7 @@ struct Cfg {
   static constexpr int EC = BN >= 128 ? 128 : BN;  // columns per epilogue warp
   static constexpr int EPI_WARPS = 4 * (BN / EC);
   static constexpr int OUT_STAGE_BYTES = EPI_WARPS * 4096;  // one 32x32 fp32 block per epilogue warp
-  static constexpr int SMEM_BYTES = RING_BYTES + OUT_STAGE_BYTES + 1024 + 256;
+  static constexpr int SMEM_BYTES = RING_BYTES + OUT_STAGE_BYTES + 1024 + 512;
   static constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int NBUF = 512 / BN;  // TMEM accumulator buffers (chunks in flight)
   static constexpr uint32_t TMEM_COLS = 512;
@@ -62,7 +68,7 @@ struct Cfg {
       (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
-constexpr int CHUNK_KB_DEFAULT = 4;      // K blocks per TMEM accumulation chunk
+constexpr int CHUNK_KB_DEFAULT = 8;      // K blocks per TMEM accumulation chunk (128 k)
 constexpr int GROUP_M = 8;
 
 struct TcEpi {
@@ -219,9 +225,10 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
             const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
 #pragma unroll
             for (int kk = 0; kk < BK / 8; kk++) {
-              const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle atom
-              const uint64_t ah = make_desc(base + off), al = make_desc(base + TILE_A + off);
-              const uint64_t bh = make_desc(base + 2 * TILE_A + off), bl = make_desc(base + 2 * TILE_A + TILE_B + off);
+              const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the 64-byte row
+              const uint64_t ah = make_desc_sw64(base + off), al = make_desc_sw64(base + TILE_A + off);
+              const uint64_t bh = make_desc_sw64(base + 2 * TILE_A + off),
+                             bl = make_desc_sw64(base + 2 * TILE_A + TILE_B + off);
               const uint32_t first = (kb == c * CHUNK_KB && kk == 0) ? 0u : 1u;
               mma_tf32(dacc, al, bh, C::IDESC, first);  // small terms first
               mma_tf32(dacc, ah, bl, C::IDESC, 1u);
@@ -443,7 +450,7 @@ __global__ void __launch_bounds__(256) split_contig(const float *__restrict__ sr
 }
 
 // ---------------------------------------------------------------- host side
-int64_t padded_k(int64_t K) { return ((K + BK - 1) / BK) * BK; }
+int64_t padded_k(int64_t K) { return ((K + KPAD - 1) / KPAD) * KPAD; }
 
 template <int BN>
 silcu_status launch_tc(const TcParams &p, uint32_t grid, cudaStream_t s) {
@@ -509,8 +516,8 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
   int launches = 0;
   // A as rows m, K-major.
   if (asplit) {
-    if (!make_map4(&p.a_hi, a.A_hi, a.K, a.M, a.lda, bin, a.stride_a_inner, bout, a.stride_a, BK, BM) ||
-        !make_map4(&p.a_lo, a.A_lo, a.K, a.M, a.lda, bin, a.stride_a_inner, bout, a.stride_a, BK, BM))
+    if (!make_map4(&p.a_hi, a.A_hi, a.K, a.M, a.lda, bin, a.stride_a_inner, bout, a.stride_a, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map4(&p.a_lo, a.A_lo, a.K, a.M, a.lda, bin, a.stride_a_inner, bout, a.stride_a, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B))
       return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed (A)");
   } else {
     const size_t el = size_t(nb) * a.M * Kp;
@@ -529,14 +536,14 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
       pack_split<<<g, 256, 0, s>>>(src, src_lo, rs, ks, a.stride_a, bin, a.stride_a_inner, a.M, a.K, Kp, hi, lo);
     }
     launches++;
-    if (!make_map4(&p.a_hi, hi, Kp, a.M, Kp, bin, a.M * Kp, bout, bin * a.M * Kp, BK, BM) ||
-        !make_map4(&p.a_lo, lo, Kp, a.M, Kp, bin, a.M * Kp, bout, bin * a.M * Kp, BK, BM))
+    if (!make_map4(&p.a_hi, hi, Kp, a.M, Kp, bin, a.M * Kp, bout, bin * a.M * Kp, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map4(&p.a_lo, lo, Kp, a.M, Kp, bin, a.M * Kp, bout, bin * a.M * Kp, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B))
       return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed (A pack)");
   }
   // B as rows n, K-major.  Non-transposed B [K,N]: (n, k) at k*ldb + n.  Transposed [N,K]: n*ldb + k.
   if (bsplit) {
-    if (!make_map4(&p.b_hi, a.B_hi, a.K, a.N, a.ldb, bin, a.stride_b_inner, bout, a.stride_b, BK, BN) ||
-        !make_map4(&p.b_lo, a.B_lo, a.K, a.N, a.ldb, bin, a.stride_b_inner, bout, a.stride_b, BK, BN))
+    if (!make_map4(&p.b_hi, a.B_hi, a.K, a.N, a.ldb, bin, a.stride_b_inner, bout, a.stride_b, BK, BN, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map4(&p.b_lo, a.B_lo, a.K, a.N, a.ldb, bin, a.stride_b_inner, bout, a.stride_b, BK, BN, CU_TENSOR_MAP_SWIZZLE_64B))
       return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed (B)");
   } else {
     const size_t el = size_t(nb) * a.N * Kp;
@@ -548,8 +555,8 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
     dim3 g(uint32_t(Kp / 32), uint32_t((a.N + 31) / 32), uint32_t(nb));
     pack_split<<<g, 256, 0, s>>>(src, src_lo, rs, ks, a.stride_b, bin, a.stride_b_inner, a.N, a.K, Kp, hi, lo);
     launches++;
-    if (!make_map4(&p.b_hi, hi, Kp, a.N, Kp, bin, a.N * Kp, bout, bin * a.N * Kp, BK, BN) ||
-        !make_map4(&p.b_lo, lo, Kp, a.N, Kp, bin, a.N * Kp, bout, bin * a.N * Kp, BK, BN))
+    if (!make_map4(&p.b_hi, hi, Kp, a.N, Kp, bin, a.N * Kp, bout, bin * a.N * Kp, BK, BN, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map4(&p.b_lo, lo, Kp, a.N, Kp, bin, a.N * Kp, bout, bin * a.N * Kp, BK, BN, CU_TENSOR_MAP_SWIZZLE_64B))
       return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed (B pack)");
   }
   if (launches) {
