@@ -21,7 +21,8 @@
 //               nearest), and at the end of a tile stage 32x32 blocks through
 //               shared memory so that the alpha / bias / activation / residual
 //               epilogue and the stores are coalesced 128-byte row segments.
-// No TMA multicast and no clusters: each CTA loads its own tiles.
+// Each CTA loads its own tiles (no TMA multicast); large problems run as CTA
+// pairs (tcgen05 cta_group::2, 256-row tiles), see tc_gemm_kernel.
 // Every mbarrier wait is bounded (wall-clock limit via %globaltimer); on
 // expiry it records an error in the device error word and the CTA unwinds,
 // frees its TMEM and exits.
@@ -48,24 +49,31 @@ constexpr int KPAD = 32;  // K padding of the split copies written by the pre-pa
 // k keep several TMA fills in flight while the MMAs consume one: a stage of
 // 32 k at BN = 256 (96 KB) left room for only two, and the fill latency
 // showed up as idle tensor cycles.
-template <int BN_>
+template <int BN_, bool PAIR_ = false>
 struct Cfg {
   static constexpr int BN = BN_;
+  static constexpr bool PAIR = PAIR_;
+  static constexpr int TM = PAIR ? 2 * BM : BM;       // output rows per tile (a CTA pair: 256)
+  static constexpr int ROWS_B = PAIR ? BN / 2 : BN;   // B rows (K-major copy) held per CTA
   static constexpr int TILE_A = BM * BK * 4;
-  static constexpr int TILE_B = BN * BK * 4;
+  static constexpr int TILE_B = ROWS_B * BK * 4;
   static constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_B;  // Ahi, Alo, Bhi, Blo
-  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
-  static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
   static constexpr int EC = BN >= 128 ? 128 : BN;  // columns per epilogue warp
   static constexpr int EPI_WARPS = 4 * (BN / EC);
-  static constexpr int OUT_STAGE_BYTES = EPI_WARPS * 4096;  // one 32x32 fp32 block per epilogue warp
+  // 32x32 fp32 staging blocks per epilogue warp: pairs (smaller stages) can
+  // afford two, so consecutive TMA stores overlap.
+  static constexpr int OUT_BUFS = PAIR ? 2 : 1;
+  static constexpr int OUT_STAGE_BYTES = EPI_WARPS * 4096 * OUT_BUFS;
+  static constexpr int STAGES_FIT = (232448 - OUT_STAGE_BYTES - 1024 - 512) / STAGE_BYTES;
+  static constexpr int STAGES = PAIR ? (STAGES_FIT < 8 ? STAGES_FIT : 8) : (192 * 1024) / STAGE_BYTES;
+  static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
   static constexpr int SMEM_BYTES = RING_BYTES + OUT_STAGE_BYTES + 1024 + 512;
   static constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int NBUF = 512 / BN;  // TMEM accumulator buffers (chunks in flight)
   static constexpr uint32_t TMEM_COLS = 512;
   // Instruction descriptor: D fp32, A/B tf32, both K-major, N = BN, M = BM.
   static constexpr uint32_t IDESC =
-      (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+      (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(TM >> 4) << 24);
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 constexpr int CHUNK_KB_DEFAULT = 8;      // K blocks per TMEM accumulation chunk (128 k)
@@ -97,7 +105,7 @@ struct Tile {
 
 // Grouped raster inside one batch: GROUP_M tile-rows sweep the N tiles
 // together so the A and B strips they share stay in L2.
-template <int BN>
+template <int TM, int BN>
 __device__ __forceinline__ Tile decode_tile(const TcParams &p, int idx) {
   const int tiles_per_batch = p.tiles_m * p.tiles_n;
   Tile r;
@@ -108,7 +116,7 @@ __device__ __forceinline__ Tile decode_tile(const TcParams &p, int idx) {
   const int gm = min(p.tiles_m - first_m, GROUP_M);
   const int tm = first_m + (t % (GROUP_M * p.tiles_n)) % gm;
   const int tn = (t % (GROUP_M * p.tiles_n)) / gm;
-  r.m0 = tm * BM;
+  r.m0 = tm * TM;
   r.n0 = tn * BN;
   return r;
 }
@@ -143,9 +151,16 @@ __device__ __forceinline__ void stage_row_swz(float *st, int lane, const float (
 // accumulate into one of NBUF TMEM buffers; the epilogue warps drain each
 // finished chunk into fp32 registers with round-to-nearest adds while the
 // MMAs continue in the other buffers.
-template <int BN_>
+//
+// PAIR (a cluster of two CTAs on one TPC, tcgen05 cta_group::2): the pair
+// computes 256 x BN tiles.  Each CTA loads its own 128 rows of A and half of
+// the BN columns of B; the even CTA issues M = 256 MMAs that read both CTAs'
+// shared memory and write each CTA's TMEM, waits on its own ring barriers
+// (which also count the peer's TMA bytes) and commits to the barriers of both
+// CTAs; both CTAs' epilogue warps release the accumulator buffers to it.
+template <int BN_, bool PAIR>
 __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
-  using C = Cfg<BN_>;
+  using C = Cfg<BN_, PAIR>;
   constexpr int BN = C::BN, STAGES = C::STAGES, NBUF = C::NBUF, RING_BYTES = C::RING_BYTES;
   constexpr int STAGE_BYTES = C::STAGE_BYTES, TILE_A = C::TILE_A, TILE_B = C::TILE_B;
   constexpr uint32_t TMEM_COLS = C::TMEM_COLS;
@@ -159,6 +174,9 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total_tiles = p.tiles_m * p.tiles_n * p.nbatch;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int first_tile = PAIR ? int(blockIdx.x >> 1) : int(blockIdx.x);
+  const int tile_step = PAIR ? int(gridDim.x >> 1) : int(gridDim.x);
   const int nk = (p.K + BK - 1) / BK;
   const int CHUNK_KB = p.chunk_kb;
   const int nchunks = (nk + CHUNK_KB - 1) / CHUNK_KB;
@@ -170,17 +188,24 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
     }
     for (int j = 0; j < NBUF; j++) {
       mbar_init(tfull0 + 8 * j, 1);
-      mbar_init(tempty0 + 8 * j, C::EPI_WARPS);  // one arrive per epilogue warp
+      mbar_init(tempty0 + 8 * j, C::EPI_WARPS * (PAIR ? 2 : 1));  // one arrive per epilogue warp (of both CTAs)
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(TMEM_COLS));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(TMEM_COLS));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync_all();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -188,29 +213,40 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
     if (lane == 0) {
       uint32_t kbg = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
-        const Tile tl = decode_tile<BN>(p, tile);
+      for (int tile = first_tile; tile < total_tiles && ok; tile += tile_step) {
+        const Tile tl = decode_tile<C::TM, BN>(p, tile);
         const int bo = tl.bz / p.bin, bi = tl.bz % p.bin;
+        const int am = tl.m0 + BM * int(rank), bn = tl.n0 + C::ROWS_B * int(rank);
         for (int kb = 0; kb < nk; kb++, kbg++) {
           const uint32_t s = kbg % STAGES;
           const uint32_t ph = (kbg / STAGES) & 1;
           if (kbg >= STAGES && !mbar_wait(empty0 + 8 * s, ph ^ 1, p.err, 1)) { ok = false; break; }
           const uint32_t full = full0 + 8 * s;
-          mbar_expect_tx(full, STAGE_BYTES);
           const uint32_t dst = smem_u32(smem + s * STAGE_BYTES);
           const int kc = kb * BK;
-          tma_load_4d(dst, &p.a_hi, full, kc, tl.m0, bi, bo);
-          tma_load_4d(dst + TILE_A, &p.a_lo, full, kc, tl.m0, bi, bo);
-          tma_load_4d(dst + 2 * TILE_A, &p.b_hi, full, kc, tl.n0, bi, bo);
-          tma_load_4d(dst + 2 * TILE_A + TILE_B, &p.b_lo, full, kc, tl.n0, bi, bo);
+          if (PAIR) {
+            // Both CTAs' bytes complete on the even CTA's barrier, which expects them all.
+            const uint32_t full_c = mapa_shared(full, 0);
+            if (rank == 0) mbar_expect_tx(full, 2 * STAGE_BYTES);
+            tma_load_4d_pair(dst, &p.a_hi, full_c, kc, am, bi, bo);
+            tma_load_4d_pair(dst + TILE_A, &p.a_lo, full_c, kc, am, bi, bo);
+            tma_load_4d_pair(dst + 2 * TILE_A, &p.b_hi, full_c, kc, bn, bi, bo);
+            tma_load_4d_pair(dst + 2 * TILE_A + TILE_B, &p.b_lo, full_c, kc, bn, bi, bo);
+          } else {
+            mbar_expect_tx(full, STAGE_BYTES);
+            tma_load_4d(dst, &p.a_hi, full, kc, am, bi, bo);
+            tma_load_4d(dst + TILE_A, &p.a_lo, full, kc, am, bi, bo);
+            tma_load_4d(dst + 2 * TILE_A, &p.b_hi, full, kc, bn, bi, bo);
+            tma_load_4d(dst + 2 * TILE_A + TILE_B, &p.b_lo, full, kc, bn, bi, bo);
+          }
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {  // the pair's MMAs are issued by the even CTA
       uint32_t kbg = 0, cg = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+      for (int tile = first_tile; tile < total_tiles && ok; tile += tile_step) {
         for (int c = 0; c < nchunks && ok; c++, cg++) {
           const uint32_t j = cg % NBUF, use = cg / NBUF;
           if (cg >= NBUF && !mbar_wait(tempty0 + 8 * j, (use & 1) ^ 1, p.err, 4)) { ok = false; break; }
@@ -230,13 +266,29 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
               const uint64_t bh = make_desc_sw64(base + 2 * TILE_A + off),
                              bl = make_desc_sw64(base + 2 * TILE_A + TILE_B + off);
               const uint32_t first = (kb == c * CHUNK_KB && kk == 0) ? 0u : 1u;
-              mma_tf32(dacc, al, bh, C::IDESC, first);  // small terms first
-              mma_tf32(dacc, ah, bl, C::IDESC, 1u);
-              mma_tf32(dacc, ah, bh, C::IDESC, 1u);
+              if (PAIR) {
+                mma_tf32_pair(dacc, al, bh, C::IDESC, first);  // small terms first
+                mma_tf32_pair(dacc, ah, bl, C::IDESC, 1u);
+                mma_tf32_pair(dacc, ah, bh, C::IDESC, 1u);
+              } else {
+                mma_tf32(dacc, al, bh, C::IDESC, first);  // small terms first
+                mma_tf32(dacc, ah, bl, C::IDESC, 1u);
+                mma_tf32(dacc, ah, bh, C::IDESC, 1u);
+              }
             }
-            mma_commit(empty0 + 8 * s);
+            if (PAIR) {  // the stage is free in both CTAs
+              mma_commit_pair(empty0 + 8 * s);
+              mma_commit_pair(mapa_shared(empty0 + 8 * s, 1));
+            } else {
+              mma_commit(empty0 + 8 * s);
+            }
           }
-          mma_commit(tfull0 + 8 * j);  // fires when this chunk's MMAs have completed
+          if (PAIR) {  // fires when this chunk's MMAs have completed, in both CTAs
+            mma_commit_pair(tfull0 + 8 * j);
+            mma_commit_pair(mapa_shared(tfull0 + 8 * j, 1));
+          } else {
+            mma_commit(tfull0 + 8 * j);
+          }
         }
       }
     }
@@ -245,12 +297,13 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
     // 32q..32q+31; warp group h = (warp - 2) / 4 owns columns 128h..128h+127.
     const int q = warp & 3;
     const int h = (warp - 2) >> 2;
-    float *st = ostage + (warp - 2) * 1024;
-    const uint32_t st_addr = smem_u32(st);
+    float *st = ostage + (warp - 2) * 1024 * C::OUT_BUFS;
+    uint32_t nstore = 0;
     uint32_t cg = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
-      const Tile tl = decode_tile<BN>(p, tile);
+    for (int tile = first_tile; tile < total_tiles && ok; tile += tile_step) {
+      const Tile tl = decode_tile<C::TM, BN>(p, tile);
+      const int m0 = tl.m0 + BM * int(rank);  // this CTA's 128 rows of the tile
       constexpr int EC = C::EC;
       float acc[EC];
 #pragma unroll
@@ -276,7 +329,10 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(tempty0 + 8 * j);
+        if (lane == 0) {
+          if (PAIR) mbar_arrive_cluster(mapa_shared(tempty0 + 8 * j, 0));  // the MMA issuer's barrier
+          else mbar_arrive(tempty0 + 8 * j);
+        }
       }
       const bool good = __all_sync(0xffffffffu, ok && *reinterpret_cast<volatile int *>(p.err) == 0);
       if (!good) break;
@@ -284,7 +340,7 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
       // residual, in the reference's order; then 32x32 blocks leave through
       // shared memory (TMA stores, or a transposed coalesced store fallback).
       const int bo = tl.bz / p.bin, bi = tl.bz % p.bin;
-      const int row = tl.m0 + 32 * q + lane;
+      const int row = m0 + 32 * q + lane;
       const int64_t coff = int64_t(bo) * p.stride_c + int64_t(bi) * p.stride_c_in;
 #pragma unroll
       for (int cb = 0; cb < EC / 32; cb++) {
@@ -326,22 +382,28 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
               if (col0 + i < p.N) acc[32 * cb + i] = __fadd_rn(acc[32 * cb + i], __ldg(rp + i));
           }
         }
+        if (m0 + 32 * q >= p.M) continue;  // a pair's second half past M: nothing to store
         if (p.tma_c || p.split_out) {
           // up to three outputs leave through the one staging block
 #pragma unroll 1
           for (int o = 0; o < 3; o++) {
             if (o == 0 && !p.tma_c) continue;
             if (o > 0 && !p.split_out) break;
-            if (lane == 0) bulk_wait_read0();  // the previous store has read the block
+            float *sb = st + (C::OUT_BUFS == 2 ? (nstore & 1) * 1024 : 0);
+            if (lane == 0) {  // the store that last used this block has read it
+              if (C::OUT_BUFS == 2) bulk_wait_read1();
+              else bulk_wait_read0();
+            }
             __syncwarp();
-            stage_row_swz(st, lane, acc, 32 * cb, o);
+            stage_row_swz(sb, lane, acc, 32 * cb, o);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
               const CUtensorMap *m = o == 0 ? &p.c_map : (o == 1 ? &p.chi_map : &p.clo_map);
-              tma_store_4d(m, st_addr, col0, tl.m0 + 32 * q, bi, bo);
+              tma_store_4d(m, smem_u32(sb), col0, m0 + 32 * q, bi, bo);
               bulk_commit();
             }
+            nstore++;
           }
         } else {
           // Fallback (C not TMA-compatible): transpose through the staging
@@ -355,7 +417,7 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
             float *cp = p.C + coff + c;
 #pragma unroll 4
             for (int r = 0; r < 32; r++) {
-              const int rr = tl.m0 + 32 * q + r;
+              const int rr = m0 + 32 * q + r;
               if (rr < p.M) cp[int64_t(rr) * p.ldc] = st[r * 32 + (lane ^ r)];
             }
           }
@@ -368,9 +430,13 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync_all();  // no CTA frees TMEM or leaves while its peer may still use the pair
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    if (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
   }
 }
 
@@ -452,20 +518,45 @@ __global__ void __launch_bounds__(256) split_contig(const float *__restrict__ sr
 // ---------------------------------------------------------------- host side
 int64_t padded_k(int64_t K) { return ((K + KPAD - 1) / KPAD) * KPAD; }
 
-template <int BN>
+template <int BN, bool PAIR>
 silcu_status launch_tc(const TcParams &p, uint32_t grid, cudaStream_t s) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, PAIR>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e =
-        cudaFuncSetAttribute(tc_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::SMEM_BYTES);
     if (e != cudaSuccess) return fail(SILCU_CUDA_ERROR, "sgemm(tc): smem attribute: %s", cudaGetErrorString(e));
     configured[dev] = true;
   }
-  tc_gemm_kernel<BN><<<grid, C::NUM_THREADS, C::SMEM_BYTES, s>>>(p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(C::NUM_THREADS);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = PAIR ? 2 : 1;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, PAIR>, p);
+  if (e != cudaSuccess) return fail(SILCU_CUDA_ERROR, "sgemm(tc): launch: %s", cudaGetErrorString(e));
   return check_launch("sgemm(tc)");
+}
+
+// CTA pairs (256-row tiles) when there are enough of them to occupy every
+// SM pair; SILCU_TC_PAIR = 0 / 1 forces the choice (tuning).
+bool use_pair(int64_t M, int64_t tiles_n, int64_t nb) {
+  static const int forced = [] {
+    const char *e = getenv("SILCU_TC_PAIR");
+    return e ? atoi(e) : -1;
+  }();
+  if (forced == 0 || forced == 1) return forced == 1 && M >= 2 * BM;
+  const int64_t pair_tiles = (M + 2 * BM - 1) / (2 * BM) * tiles_n * nb;
+  return M >= 2 * BM && pair_tiles >= sm_count() / 2;
 }
 
 bool a_given_split(const silcu_gemm_args &a) { return a.A_hi && a.A_lo; }
@@ -491,8 +582,12 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
   if (a.M > (1 << 30) || a.N > (1 << 30) || Kp > (1 << 30))
     return fail(SILCU_UNSUPPORTED, "sgemm(tc): extent >= 2^30");
   const int BN = a.N > 128 ? 256 : (a.N > 64 ? 128 : 64);  // wide tiles unless N is small
-  const int64_t tiles_m = (a.M + BM - 1) / BM, tiles_n = (a.N + BN - 1) / BN;
+  const int64_t tiles_n = (a.N + BN - 1) / BN;
   const int64_t nb = total_batch(a), bin = a.batch_inner > 1 ? a.batch_inner : 1, bout = a.batch;
+  const bool pair = use_pair(a.M, tiles_n, nb);
+  const int TM = pair ? 2 * BM : BM;
+  const int ROWS_B = pair ? BN / 2 : BN;
+  const int64_t tiles_m = (a.M + TM - 1) / TM;
   if (tiles_m * tiles_n * nb > 0x7FFFFFFF) return fail(SILCU_UNSUPPORTED, "sgemm(tc): too many tiles");
   if (nb > 65535) return fail(SILCU_UNSUPPORTED, "sgemm(tc): batch > 65535");
   const bool asplit = a_given_split(a), bsplit = b_given_split_kmajor(a);
@@ -542,8 +637,8 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
   }
   // B as rows n, K-major.  Non-transposed B [K,N]: (n, k) at k*ldb + n.  Transposed [N,K]: n*ldb + k.
   if (bsplit) {
-    if (!make_map4(&p.b_hi, a.B_hi, a.K, a.N, a.ldb, bin, a.stride_b_inner, bout, a.stride_b, BK, BN, CU_TENSOR_MAP_SWIZZLE_64B) ||
-        !make_map4(&p.b_lo, a.B_lo, a.K, a.N, a.ldb, bin, a.stride_b_inner, bout, a.stride_b, BK, BN, CU_TENSOR_MAP_SWIZZLE_64B))
+    if (!make_map4(&p.b_hi, a.B_hi, a.K, a.N, a.ldb, bin, a.stride_b_inner, bout, a.stride_b, BK, ROWS_B, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map4(&p.b_lo, a.B_lo, a.K, a.N, a.ldb, bin, a.stride_b_inner, bout, a.stride_b, BK, ROWS_B, CU_TENSOR_MAP_SWIZZLE_64B))
       return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed (B)");
   } else {
     const size_t el = size_t(nb) * a.N * Kp;
@@ -555,8 +650,8 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
     dim3 g(uint32_t(Kp / 32), uint32_t((a.N + 31) / 32), uint32_t(nb));
     pack_split<<<g, 256, 0, s>>>(src, src_lo, rs, ks, a.stride_b, bin, a.stride_b_inner, a.N, a.K, Kp, hi, lo);
     launches++;
-    if (!make_map4(&p.b_hi, hi, Kp, a.N, Kp, bin, a.N * Kp, bout, bin * a.N * Kp, BK, BN, CU_TENSOR_MAP_SWIZZLE_64B) ||
-        !make_map4(&p.b_lo, lo, Kp, a.N, Kp, bin, a.N * Kp, bout, bin * a.N * Kp, BK, BN, CU_TENSOR_MAP_SWIZZLE_64B))
+    if (!make_map4(&p.b_hi, hi, Kp, a.N, Kp, bin, a.N * Kp, bout, bin * a.N * Kp, BK, ROWS_B, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map4(&p.b_lo, lo, Kp, a.N, Kp, bin, a.N * Kp, bout, bin * a.N * Kp, BK, ROWS_B, CU_TENSOR_MAP_SWIZZLE_64B))
       return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed (B pack)");
   }
   if (launches) {
@@ -596,10 +691,17 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
   p.err = device_error_ptr();
   if (!p.err) return fail(SILCU_CUDA_ERROR, "sgemm(tc): no device error word");
   const int64_t total = tiles_m * tiles_n * nb;
+  if (pair) {
+    const int64_t pairs = sm_count() / 2;
+    const uint32_t grid = uint32_t(2 * (total < pairs ? total : pairs));
+    if (BN == 256) return launch_tc<256, true>(p, grid, s);
+    if (BN == 128) return launch_tc<128, true>(p, grid, s);
+    return launch_tc<64, true>(p, grid, s);
+  }
   const uint32_t grid = uint32_t(total < sm_count() ? total : sm_count());
-  if (BN == 256) return launch_tc<256>(p, grid, s);
-  if (BN == 128) return launch_tc<128>(p, grid, s);
-  return launch_tc<64>(p, grid, s);
+  if (BN == 256) return launch_tc<256, false>(p, grid, s);
+  if (BN == 128) return launch_tc<128, false>(p, grid, s);
+  return launch_tc<64, false>(p, grid, s);
 }
 
 }  // namespace silcu
