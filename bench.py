@@ -467,7 +467,7 @@ def run_ours(args):
             traffic = json.load(open(traffic_path)).get("tc_gemm_kernel_ffn_up")
             if traffic is not None and T != 16384:
                 traffic = traffic * T / 16384.0
-        roofline = {"bound": "tensor", "kernel": "tc_gemm_kernel<256> M=%d N=%d K=%d (FFN-up of the forward)" % (T, f, d),
+        roofline = {"bound": "tensor", "kernel": "tc_gemm_kernel<256, pair> M=%d N=%d K=%d (FFN-up of the forward)" % (T, f, d),
                     "achieved": achieved, "peak": ceiling, "unit": "TFLOP/s", "frac": achieved / ceiling,
                     "traffic": traffic,
                     "peak_note": f"3xTF32 ceiling = {src} bf16 {bf16} TFLOP/s / 2 (tf32 rate) / 3 (MMAs per product)",
