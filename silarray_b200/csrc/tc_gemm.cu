@@ -559,6 +559,21 @@ bool use_pair(int64_t M, int64_t tiles_n, int64_t nb) {
   return M >= 2 * BM && pair_tiles >= sm_count() / 2;
 }
 
+// Tile width: the widest that N needs.  Narrower tiles never pay for a
+// better-filled last wave: measured per FLOP, BN = 128 costs ~1.7x and
+// BN = 64 ~3x the time of BN = 256 (the single MMA-issuing thread, not the
+// tensor core, bounds small-N MMAs).  SILCU_TC_BN = 64 / 128 / 256 forces
+// the width (tuning).
+int pick_bn(int64_t N) {
+  static const int forced = [] {
+    const char *e = getenv("SILCU_TC_BN");
+    const int v = e ? atoi(e) : 0;
+    return (v == 64 || v == 128 || v == 256) ? v : 0;
+  }();
+  if (forced) return forced;
+  return N > 128 ? 256 : (N > 64 ? 128 : 64);
+}
+
 bool a_given_split(const silcu_gemm_args &a) { return a.A_hi && a.A_lo; }
 bool b_given_split_kmajor(const silcu_gemm_args &a) { return a.B_hi && a.B_lo && a.trans_b; }
 
@@ -581,10 +596,10 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
     return fail(SILCU_WORKSPACE_TOO_SMALL, "sgemm(tc): workspace %zu < %zu", wsb, need);
   if (a.M > (1 << 30) || a.N > (1 << 30) || Kp > (1 << 30))
     return fail(SILCU_UNSUPPORTED, "sgemm(tc): extent >= 2^30");
-  const int BN = a.N > 128 ? 256 : (a.N > 64 ? 128 : 64);  // wide tiles unless N is small
-  const int64_t tiles_n = (a.N + BN - 1) / BN;
   const int64_t nb = total_batch(a), bin = a.batch_inner > 1 ? a.batch_inner : 1, bout = a.batch;
-  const bool pair = use_pair(a.M, tiles_n, nb);
+  const bool pair = use_pair(a.M, (a.N + 255) / 256, nb);
+  const int BN = pick_bn(a.N);
+  const int64_t tiles_n = (a.N + BN - 1) / BN;
   const int TM = pair ? 2 * BM : BM;
   const int ROWS_B = pair ? BN / 2 : BN;
   const int64_t tiles_m = (a.M + TM - 1) / TM;

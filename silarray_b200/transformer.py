@@ -118,30 +118,93 @@ class Block:
         self.r1 = e(T * d)
         self.ff = pair(T * f)
         self.scale = float(np.float32(1.0) / np.sqrt(np.float32(cfg.head_dim)))
+        self._x_dev = None  # device staging of forward_host, made on first use
 
     def forward(self, x, out=None):
+        """One block forward of all cfg.batch sequences; x and out are device
+        tensors of cfg.tokens x d_model."""
         cfg = self.cfg
-        T, d, f, S, H, hd, B = cfg.tokens, cfg.d_model, cfg.d_ff, cfg.seq, cfg.heads, cfg.head_dim, cfg.batch
         x = x.reshape(-1)
-        out = torch.empty(T * d, dtype=torch.float32, device=self.dev) if out is None else out
-        qh, ql = self.qkv
-        gpu.layer_norm_split(x, self.g1, self.be1, T, d, cfg.eps, *self.h)
-        gpu.gemm(self.h, self.wqkv_t, M=T, N=3 * d, K=d, trans_b=True, bias=self.bqkv,
-                 no_c=True, C_split=self.qkv)
+        out = torch.empty(cfg.tokens * cfg.d_model, dtype=torch.float32, device=self.dev) if out is None else out
+        self._forward_seqs(x, out.reshape(-1), 0, cfg.batch)
+        return out.reshape(cfg.tokens, cfg.d_model)
+
+    def forward_host(self, x_host, out_host, chunks=2):
+        """The forward from host memory to host memory: the batch runs in
+        `chunks` groups of sequences, and the copy of group c + 1 to the device
+        and of group c - 1 back to the host overlap the compute of group c
+        (three streams: copy in, compute = the current stream, copy out; pinned
+        host buffers of cfg.tokens x d_model floats).  Ordered on the current
+        stream: when it completes, out_host holds the result.  Two groups is
+        the measured optimum at the bench shape: more groups hide more of the
+        copies but shrink the GEMMs' M until their last wave runs mostly empty."""
+        cfg = self.cfg
+        S, d, B = cfg.seq, cfg.d_model, cfg.batch
+        if not (x_host.is_pinned() and out_host.is_pinned()):
+            raise ValueError("forward_host needs pinned host buffers")
+        if x_host.numel() != cfg.tokens * d or out_host.numel() != cfg.tokens * d:
+            raise ValueError("forward_host: buffers must hold cfg.tokens x d_model floats")
+        chunks = max(1, min(int(chunks), B))
+        if self._x_dev is None:
+            self._x_dev = torch.empty(cfg.tokens * d, dtype=torch.float32, device=self.dev)
+            self._o_dev = torch.empty(cfg.tokens * d, dtype=torch.float32, device=self.dev)
+            self._s_in = torch.cuda.Stream(device=self.dev)
+            self._s_out = torch.cuda.Stream(device=self.dev)
+        xh, oh = x_host.reshape(-1), out_host.reshape(-1)
+        comp = torch.cuda.current_stream(self.dev)
+        bounds = [B * c // chunks for c in range(chunks + 1)]
+        self._s_in.wait_stream(comp)
+        self._s_out.wait_stream(comp)
+        ready = []
+        for c in range(chunks):
+            r0, r1 = bounds[c] * S * d, bounds[c + 1] * S * d
+            with torch.cuda.stream(self._s_in):
+                self._x_dev[r0:r1].copy_(xh[r0:r1], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(self._s_in)
+            ready.append(ev)
+        for c in range(chunks):
+            r0, r1 = bounds[c] * S * d, bounds[c + 1] * S * d
+            comp.wait_event(ready[c])
+            self._forward_seqs(self._x_dev, self._o_dev, bounds[c], bounds[c + 1] - bounds[c])
+            done = torch.cuda.Event()
+            done.record(comp)
+            self._s_out.wait_event(done)
+            with torch.cuda.stream(self._s_out):
+                oh[r0:r1].copy_(self._o_dev[r0:r1], non_blocking=True)
+        comp.wait_stream(self._s_out)
+        comp.wait_stream(self._s_in)
+        return out_host
+
+    def _forward_seqs(self, x, out, b0, nb):
+        """Sequences [b0, b0 + nb) of the batch: every operand and activation
+        is the view of those rows (heads of those sequences for V^T), so the
+        groups of a chunked forward share nothing."""
+        cfg = self.cfg
+        d, f, S, H, hd = cfg.d_model, cfg.d_ff, cfg.seq, cfg.heads, cfg.head_dim
+        T = nb * S
+        t0 = b0 * S
+        rows = lambda pair, w: (pair[0][t0 * w:(t0 + T) * w], pair[1][t0 * w:(t0 + T) * w])  # noqa: E731
+        xs, outs = x[t0 * d:(t0 + T) * d], out[t0 * d:(t0 + T) * d]
+        h, qkv, ctx, ff = rows(self.h, d), rows(self.qkv, 3 * d), rows(self.ctx, d), rows(self.ff, f)
+        r1 = self.r1[t0 * d:(t0 + T) * d]
+        vo = b0 * H * hd * S
+        vt = (self.vt[0][vo:vo + nb * H * hd * S], self.vt[1][vo:vo + nb * H * hd * S])
+        qh, ql = qkv
+        gpu.layer_norm_split(xs, self.g1, self.be1, T, d, cfg.eps, *h)
+        gpu.gemm(h, self.wqkv_t, M=T, N=3 * d, K=d, trans_b=True, bias=self.bqkv, no_c=True, C_split=qkv)
         # ctx[b*S + s, h*hd + j] = softmax(Q_bh . K_bh^T * scale) . V_bh, fused; Q_bh rows are
         # qkv[b*S + s, h*hd : h*hd + hd], K_bh the same at +d; V_bh^T comes split and transposed.
-        gpu.transpose_split(qh[2 * d:], S, hd, 3 * d, batch=B, heads=H, s_b=S * 3 * d, s_h=hd,
-                            src_lo=ql[2 * d:], out=self.vt)
-        gpu.attention((qh, ql), (qh[d:], ql[d:]), self.vt, Sq=S, Sk=S, batch=B, heads=H,
+        gpu.transpose_split(qh[2 * d:], S, hd, 3 * d, batch=nb, heads=H, s_b=S * 3 * d, s_h=hd,
+                            src_lo=ql[2 * d:], out=vt)
+        gpu.attention((qh, ql), (qh[d:], ql[d:]), vt, Sq=S, Sk=S, batch=nb, heads=H,
                       ldq=3 * d, sq_b=S * 3 * d, sq_h=hd, ldk=3 * d, sk_b=S * 3 * d, sk_h=hd,
                       ldv=S, sv_b=H * hd * S, sv_h=hd * S, scale=self.scale,
-                      O_split=self.ctx, ldo=d, so_b=S * d, so_h=hd)
-        gpu.gemm(self.ctx, self.wo_t, self.r1, M=T, N=d, K=d, trans_b=True, bias=self.bo, residual=x)
-        gpu.layer_norm_split(self.r1, self.g2, self.be2, T, d, cfg.eps, *self.h)
-        gpu.gemm(self.h, self.w1_t, M=T, N=f, K=d, trans_b=True, bias=self.b1, act="relu",
-                 no_c=True, C_split=self.ff)
-        gpu.gemm(self.ff, self.w2_t, out, M=T, N=d, K=f, trans_b=True, bias=self.b2, residual=self.r1)
-        return out.reshape(T, d)
+                      O_split=ctx, ldo=d, so_b=S * d, so_h=hd)
+        gpu.gemm(ctx, self.wo_t, r1, M=T, N=d, K=d, trans_b=True, bias=self.bo, residual=xs)
+        gpu.layer_norm_split(r1, self.g2, self.be2, T, d, cfg.eps, *h)
+        gpu.gemm(h, self.w1_t, M=T, N=f, K=d, trans_b=True, bias=self.b1, act="relu", no_c=True, C_split=ff)
+        gpu.gemm(ff, self.w2_t, outs, M=T, N=d, K=f, trans_b=True, bias=self.b2, residual=r1)
 
 
 def reference_forward(cfg, params, x):

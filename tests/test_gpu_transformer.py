@@ -23,3 +23,23 @@ def test_block_forward(cuda, cfg):
     ref = transformer.reference_forward(cfg, p, x)
     transformer.check_parity(out.cpu().numpy(), ref, cfg)
     gpu.device_status()
+
+
+@pytest.mark.parametrize("chunks", [1, 3, 8])
+def test_forward_host_chunks(cuda, chunks):
+    """forward_host (host buffers, copies overlapped with the compute of other
+    sequence groups) gives the device forward's result bit for bit: every
+    output element sums the same products in the same order."""
+    cfg = transformer.Config(batch=8, seq=256, d_model=256, heads=4, d_ff=1024)
+    p = transformer.init_params(cfg, seed=5)
+    x = transformer.init_input(cfg, seed=6)
+    blk = transformer.Block(cfg, p, device="cuda")
+    want = blk.forward(torch.from_numpy(x).cuda()).cpu().numpy()
+    xh = torch.from_numpy(x).pin_memory()
+    oh = torch.empty(cfg.tokens * cfg.d_model, dtype=torch.float32).pin_memory()
+    for _ in range(2):  # the second call reuses the staging buffers and streams
+        oh.zero_()
+        blk.forward_host(xh, oh, chunks=chunks)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(oh.numpy().reshape(want.shape), want)
+    gpu.device_status()
