@@ -181,6 +181,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
     }
   } else if (warp == 1) {
     if (lane == 0) {
+      // One thread issues 48 MMAs per key block, each small (N = 64), so the
+      // issue path is kept short: descriptors are built once per buffer and
+      // offset by constants (the start-address field is the low 14 bits of a
+      // descriptor, address / 16, so desc(a + o) = desc(a) + o / 16).
+      const uint64_t dq = make_desc(base + OFF_Q);
+      const uint64_t dk0 = make_desc(base + OFF_K), dv0 = make_desc(base + OFF_V);
       bool ok = mbar_wait(bar(kQFull), 0, p.err, 13);
       auto pv = [&](int i) {
         const int u = i & 1;
@@ -189,11 +195,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
         if (i >= 2 && !mbar_wait(bar(kOEmpty + u), ((i >> 1) & 1) ^ 1, p.err, 16)) return false;
         tc_fence_after();
         const uint32_t pcol = tmem + COL_P + 128 * u;
-        const uint32_t vbase = base + OFF_V + u * V_BYTES;
+        const uint64_t dv = dv0 + uint64_t((u * V_BYTES) >> 4);
 #pragma unroll
         for (int kk = 0; kk < KB / 8; kk++) {
-          const uint32_t va = vbase + (kk >> 2) * K_ATOM + (kk & 3) * 32;
-          const uint64_t vh = make_desc(va), vl = make_desc(va + 2 * K_ATOM);
+          const uint64_t vh = dv + uint64_t(((kk >> 2) * K_ATOM + (kk & 3) * 32) >> 4);
+          const uint64_t vl = vh + uint64_t((2 * K_ATOM) >> 4);
           const uint32_t ph = pcol + 8 * kk, pl = pcol + 64 + 8 * kk;
           mma_tf32_ts(tmem + COL_O + 64 * u, pl, vh, IDESC, kk == 0 ? 0u : 1u);
           mma_tf32_ts(tmem + COL_O + 64 * u, ph, vl, IDESC, 1u);
@@ -209,14 +215,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
         if (!mbar_wait(bar(kKFull + s), (j >> 1) & 1, p.err, 17)) { ok = false; break; }
         if (j >= 2 && !mbar_wait(bar(kSEmpty + s), ((j >> 1) & 1) ^ 1, p.err, 18)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t kbase = base + OFF_K + s * K_STAGE;
+        const uint64_t dk = dk0 + uint64_t((s * K_STAGE) >> 4);
 #pragma unroll
         for (int kk = 0; kk < HD / 8; kk++) {
           const uint32_t off = (kk & 3) * 32;
-          const uint32_t qa = base + OFF_Q + (kk >> 2) * Q_ATOM + off;
-          const uint32_t ka = kbase + (kk >> 2) * K_ATOM + off;
-          const uint64_t qh = make_desc(qa), ql = make_desc(qa + 2 * Q_ATOM);
-          const uint64_t kh = make_desc(ka), kl = make_desc(ka + 2 * K_ATOM);
+          const uint64_t qh = dq + uint64_t(((kk >> 2) * Q_ATOM + off) >> 4);
+          const uint64_t ql = qh + uint64_t((2 * Q_ATOM) >> 4);
+          const uint64_t kh = dk + uint64_t(((kk >> 2) * K_ATOM + off) >> 4);
+          const uint64_t kl = kh + uint64_t((2 * K_ATOM) >> 4);
           mma_tf32(tmem + 64 * s, ql, kh, IDESC, kk == 0 ? 0u : 1u);
           mma_tf32(tmem + 64 * s, qh, kl, IDESC, 1u);
           mma_tf32(tmem + 64 * s, qh, kh, IDESC, 1u);
