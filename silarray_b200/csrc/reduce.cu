@@ -9,6 +9,7 @@
 // Row ops keep the whole row on chip: each thread holds VPT float4 of the
 // row in registers, so softmax and layer_norm read HBM once and write once
 // (the reference reads the row 2-3 times: include/gpu_kernels.metal:1316-1467).
+#include <stdlib.h>
 #include <cooperative_groups.h>
 #include <float.h>
 
@@ -384,19 +385,16 @@ __global__ void __launch_bounds__(WARP ? 256 : NT) row_kernel(const RowArgs a) {
   }
 }
 
-// Long rows: a cluster of 4 CTAs shares one row (each holds a quarter in
+// Long rows: a cluster of CL CTAs shares one row (each holds 1/CL of it in
 // registers); partial maxima / sums / argmax keys meet through distributed
 // shared memory, summed in cluster-rank order on every CTA (deterministic).
-// With 256-thread CTAs several rows are in flight per SM, which a single
-// 1024-thread CTA per row cannot do.  Requires cols % 16 == 0.
-constexpr int kClusterCtas = 4;
-
-template <int OP, int VPT>
-__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256)
-    row_cluster_kernel(const RowArgs a) {
+// With small CTAs several rows are in flight per SM, which a single
+// 1024-thread CTA per row cannot do.  Requires cols % (4 * CL) == 0.
+template <int OP, int VPT, int CL, int NT>
+__global__ void __launch_bounds__(NT) row_cluster_kernel(const RowArgs a) {
   namespace cg = cooperative_groups;
   cg::cluster_group cl = cg::this_cluster();
-  constexpr int NT = 256;
+  constexpr int kClusterCtas = CL;
   __shared__ float sf[NT / 32];
   __shared__ unsigned long long sk[NT / 32];
   __shared__ float xf[2];
@@ -583,6 +581,38 @@ void launch_row_warp(const RowArgs &a, cudaStream_t s) {
   row_kernel<OP, 32, VPT, true><<<g, 256, 0, s>>>(a);
 }
 
+template <int OP, int VPT, int CL, int NT>
+cudaError_t launch_cluster_cfg(const RowArgs &a, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.rows * CL);
+  cfg.blockDim = dim3(NT);
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = CL;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, row_cluster_kernel<OP, VPT, CL, NT>, a);
+}
+
+// Rows of 8K-32K columns: CL CTAs of NT threads share a row, VPT float4 per
+// thread (cols = 4 * VPT * NT * CL).  SILCU_ROW_LONG = 2 / 4 / 8 picks the
+// cluster size (tuning; default 4).
+template <int OP>
+cudaError_t launch_row_cluster(const RowArgs &a, cudaStream_t s) {
+  static const int cl = [] {
+    const char *e = getenv("SILCU_ROW_LONG");
+    const int v = e ? atoi(e) : 4;
+    return (v == 2 || v == 4 || v == 8) ? v : 4;
+  }();
+  const bool wide = a.cols > 16384;
+  if (cl == 2) return wide ? launch_cluster_cfg<OP, 8, 2, 512>(a, s) : launch_cluster_cfg<OP, 4, 2, 512>(a, s);
+  if (cl == 8) return wide ? launch_cluster_cfg<OP, 8, 8, 128>(a, s) : launch_cluster_cfg<OP, 4, 8, 128>(a, s);
+  return wide ? launch_cluster_cfg<OP, 8, 4, 256>(a, s) : launch_cluster_cfg<OP, 4, 4, 256>(a, s);
+}
+
 template <int OP>
 silcu_status run_rows(const char *name, const RowArgs &a, silcu_stream stream) {
   if (a.rows == 0 || a.cols == 0) return SILCU_OK;
@@ -598,11 +628,10 @@ silcu_status run_rows(const char *name, const RowArgs &a, silcu_stream stream) {
   else if (vec && c <= 2048) launch_row<OP, 256, 2>(a, s);
   else if (vec && c <= 4096) launch_row<OP, 256, 4>(a, s);
   else if (vec && c <= 8192) launch_row<OP, 512, 4>(a, s);
-  else if (vec && c <= 16384 && (c % 16 == 0) && a.rows <= 0x3FFFFFFFu)
-    row_cluster_kernel<OP, 4><<<a.rows * kClusterCtas, 256, 0, s>>>(a);
-  else if (vec && c <= 32768 && (c % 16 == 0) && a.rows <= 0x3FFFFFFFu)
-    row_cluster_kernel<OP, 8><<<a.rows * kClusterCtas, 256, 0, s>>>(a);
-  else if (vec && c <= 16384) launch_row<OP, 512, 8>(a, s);
+  else if (vec && c <= 32768 && (c % 64 == 0) && a.rows <= 0x1FFFFFFFu) {
+    const cudaError_t e = launch_row_cluster<OP>(a, s);
+    if (e != cudaSuccess) return fail(SILCU_CUDA_ERROR, "%s: launch: %s", name, cudaGetErrorString(e));
+  } else if (vec && c <= 16384) launch_row<OP, 512, 8>(a, s);
   else if (vec && c <= 32768) launch_row<OP, 1024, 8>(a, s);
   else row_kernel_generic<OP><<<a.rows < 65535u * 16 ? a.rows : 65535u * 16, 512, 0, s>>>(a);
   return check_launch(name);

@@ -94,6 +94,7 @@ struct __align__(64) TcParams {
   float *C;                            // direct-store fallback when C cannot take TMA stores
   int64_t ldc, stride_c, stride_c_in;
   int M, N, K, tiles_m, tiles_n, nbatch, bin, chunk_kb;
+  int ksplit;  // > 1: each tile's K range in ksplit parts, partials stored through c_map at z = part
   int tma_c, split_out;
   TcEpi epi;
   int *err;
@@ -173,13 +174,19 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
   const uint32_t tfull0 = smem_u32(bars + 2 * STAGES), tempty0 = smem_u32(bars + 2 * STAGES + NBUF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total_tiles = p.tiles_m * p.tiles_n * p.nbatch;
+  // Work items: (tile, K part); ksplit = 1 unless the tiles alone would leave SMs idle.
+  const int total_tiles = p.tiles_m * p.tiles_n * p.nbatch * p.ksplit;
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
   const int first_tile = PAIR ? int(blockIdx.x >> 1) : int(blockIdx.x);
   const int tile_step = PAIR ? int(gridDim.x >> 1) : int(gridDim.x);
   const int nk = (p.K + BK - 1) / BK;
   const int CHUNK_KB = p.chunk_kb;
-  const int nchunks = (nk + CHUNK_KB - 1) / CHUNK_KB;
+  // K blocks [kb0, kb1) of a work item, and its number of accumulation chunks.
+  auto k_range = [&](int item, int &kb0, int &kb1) {
+    const int ks = item % p.ksplit;
+    kb0 = ks * nk / p.ksplit;
+    kb1 = (ks + 1) * nk / p.ksplit;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
@@ -214,10 +221,12 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
       uint32_t kbg = 0;
       bool ok = true;
       for (int tile = first_tile; tile < total_tiles && ok; tile += tile_step) {
-        const Tile tl = decode_tile<C::TM, BN>(p, tile);
+        const Tile tl = decode_tile<C::TM, BN>(p, tile / p.ksplit);
         const int bo = tl.bz / p.bin, bi = tl.bz % p.bin;
         const int am = tl.m0 + BM * int(rank), bn = tl.n0 + C::ROWS_B * int(rank);
-        for (int kb = 0; kb < nk; kb++, kbg++) {
+        int kbs, kbe;
+        k_range(tile, kbs, kbe);
+        for (int kb = kbs; kb < kbe; kb++, kbg++) {
           const uint32_t s = kbg % STAGES;
           const uint32_t ph = (kbg / STAGES) & 1;
           if (kbg >= STAGES && !mbar_wait(empty0 + 8 * s, ph ^ 1, p.err, 1)) { ok = false; break; }
@@ -247,13 +256,16 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
       uint32_t kbg = 0, cg = 0;
       bool ok = true;
       for (int tile = first_tile; tile < total_tiles && ok; tile += tile_step) {
+        int kbs, kbe;
+        k_range(tile, kbs, kbe);
+        const int nchunks = (kbe - kbs + CHUNK_KB - 1) / CHUNK_KB;
         for (int c = 0; c < nchunks && ok; c++, cg++) {
           const uint32_t j = cg % NBUF, use = cg / NBUF;
           if (cg >= NBUF && !mbar_wait(tempty0 + 8 * j, (use & 1) ^ 1, p.err, 4)) { ok = false; break; }
           tc_fence_after();
           const uint32_t dacc = tmem + j * BN;
-          const int kb1 = min(nk, (c + 1) * CHUNK_KB);
-          for (int kb = c * CHUNK_KB; kb < kb1; kb++, kbg++) {
+          const int kc0 = kbs + c * CHUNK_KB, kb1 = min(kbe, kc0 + CHUNK_KB);
+          for (int kb = kc0; kb < kb1; kb++, kbg++) {
             const uint32_t s = kbg % STAGES;
             const uint32_t ph = (kbg / STAGES) & 1;
             if (!mbar_wait(full0 + 8 * s, ph, p.err, 2)) { ok = false; break; }
@@ -265,7 +277,7 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
               const uint64_t ah = make_desc_sw64(base + off), al = make_desc_sw64(base + TILE_A + off);
               const uint64_t bh = make_desc_sw64(base + 2 * TILE_A + off),
                              bl = make_desc_sw64(base + 2 * TILE_A + TILE_B + off);
-              const uint32_t first = (kb == c * CHUNK_KB && kk == 0) ? 0u : 1u;
+              const uint32_t first = (kb == kc0 && kk == 0) ? 0u : 1u;
               if (PAIR) {
                 mma_tf32_pair(dacc, al, bh, C::IDESC, first);  // small terms first
                 mma_tf32_pair(dacc, ah, bl, C::IDESC, 1u);
@@ -302,8 +314,11 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
     uint32_t cg = 0;
     bool ok = true;
     for (int tile = first_tile; tile < total_tiles && ok; tile += tile_step) {
-      const Tile tl = decode_tile<C::TM, BN>(p, tile);
+      const Tile tl = decode_tile<C::TM, BN>(p, tile / p.ksplit);
       const int m0 = tl.m0 + BM * int(rank);  // this CTA's 128 rows of the tile
+      int kbs, kbe;
+      k_range(tile, kbs, kbe);
+      const int nchunks = (kbe - kbs + CHUNK_KB - 1) / CHUNK_KB;
       constexpr int EC = C::EC;
       float acc[EC];
 #pragma unroll
@@ -339,7 +354,7 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
       // Epilogue math in registers (lane = row): alpha, bias, activation,
       // residual, in the reference's order; then 32x32 blocks leave through
       // shared memory (TMA stores, or a transposed coalesced store fallback).
-      const int bo = tl.bz / p.bin, bi = tl.bz % p.bin;
+      const int bo = tl.bz / p.bin, bi = p.ksplit > 1 ? tile % p.ksplit : tl.bz % p.bin;
       const int row = m0 + 32 * q + lane;
       const int64_t coff = int64_t(bo) * p.stride_c + int64_t(bi) * p.stride_c_in;
 #pragma unroll
@@ -581,12 +596,84 @@ bool b_given_split_kmajor(const silcu_gemm_args &a) { return a.B_hi && a.B_lo &&
 
 int64_t total_batch(const silcu_gemm_args &a) { return a.batch * (a.batch_inner > 1 ? a.batch_inner : 1); }
 
+namespace {
+
+struct TcPlan {
+  bool pair;
+  int BN, TM, ksplit;
+  int64_t tiles_m, tiles_n;
+};
+
+// CTA pairs and tile width as above; split K when the tiles alone would fill
+// less than 60 % of the grid (small M with N = 768, e.g. a shard of the
+// transformer batch on 8 GPUs): up to 8 parts of at least four accumulation
+// chunks (512 k) each, batch 1 only.  Measured at M = 2048, N = 768: K = 3072
+// 111 -> 85 us in 3 parts; K = 768 would lose (37 -> 42 us), so it does not
+// split.  SILCU_TC_KSPLIT = 1 disables it, 2..8 forces the parts (tuning).
+TcPlan tc_plan(const silcu_gemm_args &a) {
+  TcPlan pl;
+  const int64_t Kp = padded_k(a.K > 0 ? a.K : 1);
+  const int64_t nb = total_batch(a);
+  pl.pair = use_pair(a.M, (a.N + 255) / 256, nb);
+  pl.BN = pick_bn(a.N);
+  pl.TM = pl.pair ? 2 * BM : BM;
+  pl.tiles_n = (a.N + pl.BN - 1) / pl.BN;
+  pl.tiles_m = (a.M + pl.TM - 1) / pl.TM;
+  pl.ksplit = 1;
+  static const int forced = [] {
+    const char *e = getenv("SILCU_TC_KSPLIT");
+    return e ? atoi(e) : 0;
+  }();
+  const int64_t units = pl.pair ? sm_count() / 2 : sm_count();
+  const int64_t tiles = pl.tiles_m * pl.tiles_n * nb;
+  const int64_t nkb = (Kp + BK - 1) / BK;
+  if (nb == 1 && forced != 1 && tiles * 10 < units * 6 && a.N % 4 == 0) {
+    int ks = int(units / tiles);
+    if (forced >= 2 && forced <= 8) ks = forced;
+    if (ks > 8) ks = 8;
+    while (ks > 1 && nkb / ks < 4 * CHUNK_KB_DEFAULT) ks--;  // short parts lose to the extra pass
+    pl.ksplit = ks;
+  }
+  return pl;
+}
+
+size_t partial_bytes(const silcu_gemm_args &a, const TcPlan &pl) {
+  return pl.ksplit > 1 ? size_t(pl.ksplit) * size_t(a.M) * size_t(a.N) * sizeof(float) + 256 : 0;
+}
+
+// Sum of the split-K partials in part order (round to nearest), then the
+// epilogue in the tensor-core kernel's order: alpha, bias, activation,
+// residual; plain and / or split (hi, lo) output.
+__global__ void __launch_bounds__(256) splitk_finish(const float *__restrict__ part, int ksplit, int64_t M, int64_t N,
+                                                     TcEpi epi, float *C, int64_t ldc, float *C_hi, float *C_lo) {
+  const int64_t total = M * N;
+  for (int64_t j = int64_t(blockIdx.x) * 256 + threadIdx.x; j < total; j += int64_t(gridDim.x) * 256) {
+    const int64_t row = j / N, col = j % N;
+    float v = part[j];
+    for (int k = 1; k < ksplit; k++) v = __fadd_rn(v, part[int64_t(k) * total + j]);
+    if (epi.alpha != 1.0f) v = __fmul_rn(v, epi.alpha);
+    if (epi.bias) v = __fadd_rn(v, epi.bias[col % epi.bias_len]);
+    if (epi.act == SILCU_ACT_RELU) v = v >= 0.0f ? v : 0.0f;
+    else if (epi.act == SILCU_ACT_SIGMOID) v = sigmoid_ref(v);
+    if (epi.residual) v = __fadd_rn(v, epi.residual[row * epi.ldr + col]);
+    const int64_t o = row * ldc + col;
+    if (C) C[o] = v;
+    if (C_hi) {
+      const float hi = tf32_rna(v);
+      C_hi[o] = hi;
+      C_lo[o] = __fsub_rn(v, hi);
+    }
+  }
+}
+
+}  // namespace
+
 size_t tc_workspace_bytes(const silcu_gemm_args &a) {
   const int64_t Kp = padded_k(a.K > 0 ? a.K : 1);
   size_t bytes = 256;
   if (!a_given_split(a)) bytes += size_t(2) * Kp * size_t(total_batch(a)) * size_t(a.M) * sizeof(float);
   if (!b_given_split_kmajor(a)) bytes += size_t(2) * Kp * size_t(total_batch(a)) * size_t(a.N) * sizeof(float);
-  return bytes;
+  return bytes + partial_bytes(a, tc_plan(a));
 }
 
 silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t s) {
@@ -597,12 +684,11 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
   if (a.M > (1 << 30) || a.N > (1 << 30) || Kp > (1 << 30))
     return fail(SILCU_UNSUPPORTED, "sgemm(tc): extent >= 2^30");
   const int64_t nb = total_batch(a), bin = a.batch_inner > 1 ? a.batch_inner : 1, bout = a.batch;
-  const bool pair = use_pair(a.M, (a.N + 255) / 256, nb);
-  const int BN = pick_bn(a.N);
-  const int64_t tiles_n = (a.N + BN - 1) / BN;
-  const int TM = pair ? 2 * BM : BM;
+  const TcPlan plan = tc_plan(a);
+  const bool pair = plan.pair;
+  const int BN = plan.BN;
+  const int64_t tiles_n = plan.tiles_n, tiles_m = plan.tiles_m;
   const int ROWS_B = pair ? BN / 2 : BN;
-  const int64_t tiles_m = (a.M + TM - 1) / TM;
   if (tiles_m * tiles_n * nb > 0x7FFFFFFF) return fail(SILCU_UNSUPPORTED, "sgemm(tc): too many tiles");
   if (nb > 65535) return fail(SILCU_UNSUPPORTED, "sgemm(tc): batch > 65535");
   const bool asplit = a_given_split(a), bsplit = b_given_split_kmajor(a);
@@ -705,18 +791,48 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
   p.epi.ldr = a.ldr;
   p.err = device_error_ptr();
   if (!p.err) return fail(SILCU_CUDA_ERROR, "sgemm(tc): no device error word");
-  const int64_t total = tiles_m * tiles_n * nb;
+  p.ksplit = plan.ksplit;
+  float *part = nullptr;
+  if (plan.ksplit > 1) {
+    // The kernel stores plain partials (part k at z = k); the epilogue runs in splitk_finish.
+    part = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(cur) + 255) & ~uintptr_t(255));
+    if (!make_map4(&p.c_map, part, a.N, a.M, a.N, plan.ksplit, a.M * a.N, 1, plan.ksplit * a.M * a.N, 32, 32))
+      return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed (split-K partials)");
+    p.tma_c = 1;
+    p.split_out = 0;
+    p.epi.alpha = 1.0f;
+    p.epi.bias = nullptr;
+    p.epi.act = SILCU_ACT_NONE;
+    p.epi.residual = nullptr;
+  }
+  const int64_t total = tiles_m * tiles_n * nb * plan.ksplit;
+  silcu_status st;
   if (pair) {
     const int64_t pairs = sm_count() / 2;
     const uint32_t grid = uint32_t(2 * (total < pairs ? total : pairs));
-    if (BN == 256) return launch_tc<256, true>(p, grid, s);
-    if (BN == 128) return launch_tc<128, true>(p, grid, s);
-    return launch_tc<64, true>(p, grid, s);
+    if (BN == 256) st = launch_tc<256, true>(p, grid, s);
+    else if (BN == 128) st = launch_tc<128, true>(p, grid, s);
+    else st = launch_tc<64, true>(p, grid, s);
+  } else {
+    const uint32_t grid = uint32_t(total < sm_count() ? total : sm_count());
+    if (BN == 256) st = launch_tc<256, false>(p, grid, s);
+    else if (BN == 128) st = launch_tc<128, false>(p, grid, s);
+    else st = launch_tc<64, false>(p, grid, s);
   }
-  const uint32_t grid = uint32_t(total < sm_count() ? total : sm_count());
-  if (BN == 256) return launch_tc<256, false>(p, grid, s);
-  if (BN == 128) return launch_tc<128, false>(p, grid, s);
-  return launch_tc<64, false>(p, grid, s);
+  if (st != SILCU_OK || plan.ksplit == 1) return st;
+  TcEpi epi;
+  epi.alpha = a.alpha;
+  epi.bias = a.bias;
+  epi.bias_len = int(a.bias_len > 0 ? a.bias_len : 1);
+  epi.act = a.act;
+  epi.residual = a.residual;
+  epi.ldr = a.ldr;
+  const int64_t n = a.M * a.N;
+  const int64_t blocks = (n + 255) / 256, cap = int64_t(sm_count()) * 8;
+  splitk_finish<<<uint32_t(blocks < cap ? blocks : cap), 256, 0, s>>>(part, plan.ksplit, a.M, a.N, epi, a.C, a.ldc,
+                                                                     split_out ? a.C_hi : nullptr,
+                                                                     split_out ? a.C_lo : nullptr);
+  return check_launch("sgemm(tc) split-K finish");
 }
 
 }  // namespace silcu
