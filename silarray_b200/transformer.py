@@ -176,6 +176,58 @@ class Block:
         comp.wait_stream(self._s_in)
         return out_host
 
+    def forward_host_stream(self, x_hosts, out_hosts):
+        """Forwards of consecutive batches from host to host, overlapped
+        across batches: while batch k computes, batch k + 1 is copied in and
+        batch k - 1 is copied out (three streams, two device buffers each for
+        input and output).  x_hosts / out_hosts are sequences of pinned host
+        buffers of cfg.tokens x d_model floats (an output buffer may be listed
+        again two or more batches later: the copies into it stay in order).
+        Ordered on the current stream: when it completes, every out_hosts[k]
+        holds the forward of x_hosts[k]."""
+        cfg = self.cfg
+        n = cfg.tokens * cfg.d_model
+        if len(x_hosts) != len(out_hosts):
+            raise ValueError("forward_host_stream: as many outputs as inputs")
+        for t in list(x_hosts) + list(out_hosts):
+            if not t.is_pinned() or t.numel() != n:
+                raise ValueError("forward_host_stream needs pinned host buffers of cfg.tokens x d_model floats")
+        if getattr(self, "_stream_bufs", None) is None:
+            e = lambda: torch.empty(n, dtype=torch.float32, device=self.dev)  # noqa: E731
+            self._stream_bufs = ([e(), e()], [e(), e()])
+            self._s_in2 = torch.cuda.Stream(device=self.dev)
+            self._s_out2 = torch.cuda.Stream(device=self.dev)
+        din, dout = self._stream_bufs
+        comp = torch.cuda.current_stream(self.dev)
+        self._s_in2.wait_stream(comp)
+        self._s_out2.wait_stream(comp)
+        computed = [None, None]  # per device buffer: the compute that last read din / wrote dout
+        copied_out = [None, None]  # per device buffer: the copy that last read dout
+        for k in range(len(x_hosts)):
+            i = k & 1
+            with torch.cuda.stream(self._s_in2):
+                if computed[i] is not None:
+                    self._s_in2.wait_event(computed[i])  # din[i] free once batch k - 2 computed
+                din[i].copy_(x_hosts[k].reshape(-1), non_blocking=True)
+                ready = torch.cuda.Event()
+                ready.record(self._s_in2)
+            comp.wait_event(ready)
+            if copied_out[i] is not None:
+                comp.wait_event(copied_out[i])  # dout[i] read out for batch k - 2
+            self._forward_seqs(din[i], dout[i], 0, cfg.batch)
+            done = torch.cuda.Event()
+            done.record(comp)
+            computed[i] = done
+            with torch.cuda.stream(self._s_out2):
+                self._s_out2.wait_event(done)
+                out_hosts[k].reshape(-1).copy_(dout[i], non_blocking=True)
+                c = torch.cuda.Event()
+                c.record(self._s_out2)
+            copied_out[i] = c
+        comp.wait_stream(self._s_out2)
+        comp.wait_stream(self._s_in2)
+        return out_hosts
+
     def _forward_seqs(self, x, out, b0, nb):
         """Sequences [b0, b0 + nb) of the batch: every operand and activation
         is the view of those rows (heads of those sequences for V^T), so the

@@ -43,3 +43,30 @@ def test_forward_host_chunks(cuda, chunks):
         torch.cuda.synchronize()
         np.testing.assert_array_equal(oh.numpy().reshape(want.shape), want)
     gpu.device_status()
+
+
+def test_forward_host_stream(cuda):
+    """Consecutive batches host to host with the copies of neighbouring
+    batches overlapping the compute: each output equals the device forward of
+    its input bit for bit, in one call over five batches and in five calls of
+    one batch whose outputs alternate between two host buffers."""
+    cfg = transformer.Config(batch=4, seq=256, d_model=256, heads=4, d_ff=1024)
+    p = transformer.init_params(cfg, seed=7)
+    blk = transformer.Block(cfg, p, device="cuda")
+    xs = [transformer.init_input(cfg, seed=10 + k) for k in range(5)]
+    want = [blk.forward(torch.from_numpy(x).cuda()).cpu().numpy() for x in xs]
+    xh = [torch.from_numpy(x).pin_memory() for x in xs]
+    oh = [torch.empty(cfg.tokens * cfg.d_model, dtype=torch.float32).pin_memory() for _ in range(5)]
+    blk.forward_host_stream(xh, oh)
+    torch.cuda.synchronize()
+    for k in range(5):
+        np.testing.assert_array_equal(oh[k].numpy().reshape(want[k].shape), want[k])
+    ring = [torch.empty(cfg.tokens * cfg.d_model, dtype=torch.float32).pin_memory() for _ in range(2)]
+    got = []
+    for k in range(5):  # one batch per call, outputs read back between calls
+        blk.forward_host_stream([xh[k]], [ring[k % 2]])
+        torch.cuda.synchronize()
+        got.append(ring[k % 2].numpy().copy())
+    for k in range(5):
+        np.testing.assert_array_equal(got[k].reshape(want[k].shape), want[k])
+    gpu.device_status()
