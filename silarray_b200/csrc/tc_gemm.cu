@@ -507,6 +507,60 @@ __global__ void __launch_bounds__(256) pack_split(const float *__restrict__ src,
 
 // Elementwise split of a contiguous K-major operand (no transposition):
 // 4 elements per thread, 128-bit loads and stores.
+// Transposing split of a pair (value = src + src_lo) for the aligned case:
+// a CTA takes 128 rows (tokens) x 32 columns (dims) of one (batch, head)
+// block, reads both arrays with 16-byte loads, transposes through padded
+// shared memory and writes hi / lo rows of 128 with 16-byte stores.  Output
+// as pack_split: element (c, r) of block z at ((z * cols + c) * rows + r).
+__global__ void __launch_bounds__(256) transpose_split_pair(const float *__restrict__ src,
+                                                            const float *__restrict__ src_lo, int64_t ld,
+                                                            int64_t s_b, int64_t s_h, int64_t heads, int64_t rows,
+                                                            int64_t cols, float *__restrict__ hi,
+                                                            float *__restrict__ lo) {
+  __shared__ float th[32][129], tl[32][129];
+  const int tid = threadIdx.x;
+  const int64_t z = blockIdx.z;
+  const int64_t r0 = int64_t(blockIdx.x) * 128, c0 = int64_t(blockIdx.y) * 32;
+  const int64_t boff = (z / heads) * s_b + (z % heads) * s_h;
+  const float *sh = src + boff, *sl = src_lo + boff;
+  const int f = tid & 7;
+  float4 vh[4], vl[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int64_t r = r0 + (tid >> 3) + 32 * i;
+    if (r < rows) {
+      vh[i] = __ldg(reinterpret_cast<const float4 *>(sh + r * ld + c0) + f);
+      vl[i] = __ldg(reinterpret_cast<const float4 *>(sl + r * ld + c0) + f);
+    } else {
+      vh[i] = vl[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int rl = (tid >> 3) + 32 * i;
+    th[4 * f + 0][rl] = vh[i].x; th[4 * f + 1][rl] = vh[i].y; th[4 * f + 2][rl] = vh[i].z; th[4 * f + 3][rl] = vh[i].w;
+    tl[4 * f + 0][rl] = vl[i].x; tl[4 * f + 1][rl] = vl[i].y; tl[4 * f + 2][rl] = vl[i].z; tl[4 * f + 3][rl] = vl[i].w;
+  }
+  __syncthreads();
+  const int q = tid & 31;
+  const int64_t r = r0 + 4 * q;
+  if (r >= rows) return;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int d = (tid >> 5) + 8 * i;
+    float x[4], h4[4], l4[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      x[e] = __fadd_rn(th[d][4 * q + e], tl[d][4 * q + e]);
+      h4[e] = tf32_rna(x[e]);
+      l4[e] = __fsub_rn(x[e], h4[e]);
+    }
+    const size_t o = size_t(z * cols + c0 + d) * size_t(rows) + size_t(r);
+    *reinterpret_cast<float4 *>(hi + o) = make_float4(h4[0], h4[1], h4[2], h4[3]);
+    *reinterpret_cast<float4 *>(lo + o) = make_float4(l4[0], l4[1], l4[2], l4[3]);
+  }
+}
+
 __global__ void __launch_bounds__(256) split_contig(const float *__restrict__ src, uint64_t n,
                                                     float *__restrict__ hi, float *__restrict__ lo) {
   const uint64_t stride = uint64_t(gridDim.x) * 256 * 4;
@@ -859,6 +913,13 @@ extern "C" silcu_status silcu_transpose_split_f32(const float *src, const float 
   if (rows > 65535ull * 32 || cols > 65535ull * 32 || batch * heads > 65535)
     return fail(SILCU_UNSUPPORTED, "transpose_split: extent too large");
   // output block (b, h) is [cols, rows]: element (c, r) = src[b*s_b + h*s_h + r*ld + c]
+  if (src_lo && cols % 32 == 0 && rows % 4 == 0 && ld % 4 == 0 && s_b % 4 == 0 && s_h % 4 == 0 && aligned16(src) &&
+      aligned16(src_lo) && aligned16(hi) && aligned16(lo)) {
+    dim3 g(uint32_t((rows + 127) / 128), uint32_t(cols / 32), uint32_t(batch * heads));
+    transpose_split_pair<<<g, 256, 0, as_stream(stream)>>>(src, src_lo, int64_t(ld), int64_t(s_b), int64_t(s_h),
+                                                          int64_t(heads), int64_t(rows), int64_t(cols), hi, lo);
+    return check_launch("transpose_split");
+  }
   const int64_t R = int64_t(cols), K = int64_t(rows);
   dim3 g(uint32_t((K + 31) / 32), uint32_t((R + 31) / 32), uint32_t(batch * heads));
   pack_split<<<g, 256, 0, as_stream(stream)>>>(src, src_lo, 1, int64_t(ld), int64_t(s_b), int64_t(heads),

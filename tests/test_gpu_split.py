@@ -37,3 +37,26 @@ def test_weight_split_transposed(cuda):
     eh, el = _split(np.ascontiguousarray(w.T))
     np.testing.assert_array_equal(hi.cpu().numpy().reshape(200, 96), eh)
     np.testing.assert_array_equal(lo.cpu().numpy().reshape(200, 96), el)
+
+
+@pytest.mark.parametrize("B,H,S,D,pair", [(2, 3, 512, 64, True), (1, 2, 100, 64, True), (2, 2, 64, 48, True),
+                                          (1, 2, 96, 64, False)])
+def test_transpose_split_heads(cuda, B, H, S, D, pair):
+    """V [B, S, H*D] (a row of all heads per token) -> per-head V^T [D, S]
+    split hi/lo, from a split pair (value = hi + lo) or a plain array: bit
+    equal to the split of the transposed value."""
+    rng = np.random.default_rng(S + D)
+    ld = H * D + 8  # padded row, as a column slice of a wider matrix
+    v = rng.normal(0, 1, (B, S, ld)).astype(np.float32)
+    vh, vl = _split(v)
+    src, src_lo = (torch.from_numpy(vh).cuda(), torch.from_numpy(vl).cuda()) if pair else \
+        (torch.from_numpy(v).cuda(), None)
+    hi = torch.empty(B * H * D * S, device="cuda")
+    lo = torch.empty(B * H * D * S, device="cuda")
+    gpu.transpose_split(src.reshape(-1), S, D, ld, batch=B, heads=H, s_b=S * ld, s_h=D,
+                        src_lo=None if src_lo is None else src_lo.reshape(-1), out=(hi, lo))
+    torch.cuda.synchronize()
+    want = np.stack([v[b, :, h * D:(h + 1) * D].T for b in range(B) for h in range(H)])
+    wh, wl = _split(np.ascontiguousarray(want))
+    np.testing.assert_array_equal(hi.cpu().numpy().reshape(want.shape), wh)
+    np.testing.assert_array_equal(lo.cpu().numpy().reshape(want.shape), wl)
