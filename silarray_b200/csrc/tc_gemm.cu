@@ -91,11 +91,12 @@ struct TcEpi {
 struct __align__(64) TcParams {
   CUtensorMap a_hi, a_lo, b_hi, b_lo;  // 4-D {K, rows, batch_inner, batch}, box {32, 128|BN, 1, 1}
   CUtensorMap c_map, chi_map, clo_map; // 4-D {N, M, batch_inner, batch}, box {32, 32, 1, 1}
+  CUtensorMap r_map;                   // the residual, same layout as C (used when tma_r)
   float *C;                            // direct-store fallback when C cannot take TMA stores
   int64_t ldc, stride_c, stride_c_in;
   int M, N, K, tiles_m, tiles_n, nbatch, bin, chunk_kb;
   int ksplit;  // > 1: each tile's K range in ksplit parts, partials stored through c_map at z = part
-  int tma_c, split_out;
+  int tma_c, split_out, tma_r;
   TcEpi epi;
   int *err;
 };
@@ -169,7 +170,8 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float *ostage = reinterpret_cast<float *>(smem + RING_BYTES);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + RING_BYTES + C::OUT_STAGE_BYTES);
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 2 * NBUF);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 2 * NBUF + C::EPI_WARPS);
+  const uint32_t rbar0 = smem_u32(bars + 2 * STAGES + 2 * NBUF);  // per epilogue warp: residual block loaded
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
   const uint32_t tfull0 = smem_u32(bars + 2 * STAGES), tempty0 = smem_u32(bars + 2 * STAGES + NBUF);
 
@@ -197,6 +199,7 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
       mbar_init(tfull0 + 8 * j, 1);
       mbar_init(tempty0 + 8 * j, C::EPI_WARPS * (PAIR ? 2 : 1));  // one arrive per epilogue warp (of both CTAs)
     }
+    for (int w = 0; w < C::EPI_WARPS; w++) mbar_init(rbar0 + 8 * w, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -311,6 +314,8 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
     const int h = (warp - 2) >> 2;
     float *st = ostage + (warp - 2) * 1024 * C::OUT_BUFS;
     uint32_t nstore = 0;
+    const uint32_t rbar = rbar0 + 8 * (warp - 2);
+    uint32_t rphase = 0;
     uint32_t cg = 0;
     bool ok = true;
     for (int tile = first_tile; tile < total_tiles && ok; tile += tile_step) {
@@ -380,7 +385,32 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
 #pragma unroll
           for (int i = 0; i < 32; i++) acc[32 * cb + i] = sigmoid_ref(acc[32 * cb + i]);
         }
-        if (p.epi.residual && row < p.M) {
+        if (p.epi.residual && p.tma_r && (p.tma_c || p.split_out)) {
+          // The warp's 32 x 32 residual block arrives by one TMA load into the
+          // staging block the output will leave through (128-byte swizzle:
+          // 16-byte chunk j of row r at j ^ (r & 7)); each lane reads its row.
+          if (m0 + 32 * q < p.M) {
+            float *sb = st + (C::OUT_BUFS == 2 ? (nstore & 1) * 1024 : 0);
+            if (lane == 0) {
+              if (C::OUT_BUFS == 2) bulk_wait_read1();
+              else bulk_wait_read0();
+              mbar_expect_tx(rbar, 4096);
+              tma_load_4d(smem_u32(sb), &p.r_map, rbar, col0, m0 + 32 * q, bi, bo);
+            }
+            const bool w = mbar_wait(rbar, rphase, p.err, 5);
+            rphase ^= 1u;
+            if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+              const float4 r4 = *reinterpret_cast<const float4 *>(sb + lane * 32 + 4 * (j ^ (lane & 7)));
+              acc[32 * cb + 4 * j] = __fadd_rn(acc[32 * cb + 4 * j], r4.x);
+              acc[32 * cb + 4 * j + 1] = __fadd_rn(acc[32 * cb + 4 * j + 1], r4.y);
+              acc[32 * cb + 4 * j + 2] = __fadd_rn(acc[32 * cb + 4 * j + 2], r4.z);
+              acc[32 * cb + 4 * j + 3] = __fadd_rn(acc[32 * cb + 4 * j + 3], r4.w);
+            }
+            __syncwarp();
+          }
+        } else if (p.epi.residual && row < p.M) {
           const float *rp = p.epi.residual + coff + int64_t(row) * p.epi.ldr + col0;
           if (col0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(rp) & 15) == 0)) {
 #pragma unroll
@@ -819,6 +849,11 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
       (!make_map4(&p.chi_map, a.C_hi, a.N, a.M, a.ldc, bin, a.stride_c_inner, bout, a.stride_c, 32, 32) ||
        !make_map4(&p.clo_map, a.C_lo, a.N, a.M, a.ldc, bin, a.stride_c_inner, bout, a.stride_c, 32, 32)))
     return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed (split C)");
+  if (a.residual && aligned_view(a.residual, a.ldr, a.stride_c_inner, a.stride_c)) {
+    if (!make_map4(&p.r_map, a.residual, a.N, a.M, a.ldr, bin, a.stride_c_inner, bout, a.stride_c, 32, 32))
+      return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed (residual)");
+    p.tma_r = 1;
+  }
   p.C = a.C;
   p.ldc = a.ldc;
   p.stride_c = a.stride_c;

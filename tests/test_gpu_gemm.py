@@ -168,18 +168,21 @@ def test_skinny_shapes_with_epilogue(cuda, M, N, K):
 def test_tc_cta_pair_ragged(cuda):
     """Large enough for CTA pairs (256-row tiles over two SMs): ragged M
     (the last pair tile's second half lies wholly past M), N and K; sampled
-    rows against fp64, bias + relu epilogue, and the split output."""
+    rows against fp64, bias + relu + residual epilogue (the residual arrives
+    by TMA), and the split output."""
     M, N, K = 3900, 2000, 700
     rng = np.random.default_rng(5)
     a = rng.uniform(-1, 1, (M, K)).astype(np.float32)
     b = rng.uniform(-1, 1, (K, N)).astype(np.float32)
     bias = rng.uniform(-1, 1, N).astype(np.float32)
+    res = rng.uniform(-1, 1, (M, N)).astype(np.float32)
     Ch = torch.empty(M * N, device="cuda")
     Cl = torch.empty(M * N, device="cuda")
-    got = gpu.gemm(dev(a), dev(b), M=M, N=N, K=K, bias=dev(bias), act="relu", algo="tc", C_split=(Ch, Cl))
+    got = gpu.gemm(dev(a), dev(b), M=M, N=N, K=K, bias=dev(bias), act="relu", residual=dev(res), algo="tc",
+                   C_split=(Ch, Cl))
     got = host(got).reshape(M, N)
     rows = [0, 1, 127, 128, 255, 256, 2000, 3839, 3840, 3871, 3899]
-    ref = np.maximum(a[rows].astype(np.float64) @ b.astype(np.float64) + bias, 0)
+    ref = np.maximum(a[rows].astype(np.float64) @ b.astype(np.float64) + bias, 0) + res[rows]
     assert_dot_close(got[rows], ref, K, what="tc pair sampled")
     hi, lo = host(Ch).reshape(M, N), host(Cl).reshape(M, N)
     np.testing.assert_array_equal((hi.astype(np.float64) + lo)[rows].astype(np.float32), got[rows])
