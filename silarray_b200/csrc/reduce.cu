@@ -531,7 +531,6 @@ __global__ void __launch_bounds__(512) row_kernel_generic(const RowArgs a) {
   const int t = threadIdx.x;
   for (uint32_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
     const float *src = a.in + size_t(row) * a.cols;
-    float *dst = a.out ? a.out + size_t(row) * a.cols : nullptr;
     if (OP == kSoftmax) {
       float m = __int_as_float(0xff800000);
       for (uint32_t c = t; c < a.cols; c += NT) m = fmaxf(m, src[c]);
