@@ -257,6 +257,11 @@ typedef struct silcu_attention_args {
 } silcu_attention_args;
 silcu_status silcu_attention_f32(const silcu_attention_args *args_host, silcu_stream stream);
 
+/* The general GEMM of the reference's dot / linear / linear_sigmoid /
+ * batched_dot nodes.  The workspace (size from silcu_sgemm_workspace_bytes,
+ * 0 when none is needed) holds the tf32 splits of operands given plain and,
+ * when a few long-K output tiles are cut into K parts, their partial sums;
+ * results are deterministic (fixed summation order). */
 size_t silcu_sgemm_workspace_bytes(const silcu_gemm_args *args_host);
 silcu_status silcu_sgemm_ex(const silcu_gemm_args *args_host, void *workspace, size_t workspace_bytes,
                             silcu_stream stream);
@@ -276,7 +281,8 @@ silcu_status silcu_sgemm_bias_sigmoid(const float *A, const float *B, float *C, 
                                       uint32_t ldb, void *workspace, size_t workspace_bytes,
                                       silcu_stream stream);
 /* gpu::sgemv (include/gpu.h:549-574): y[N] = x[K] . W[K,N] (+ bias), K split
- * across CTAs with a deterministic second pass. */
+ * across the CTAs of a thread-block cluster and combined in a fixed order
+ * (a second pass, using the workspace, only for K beyond 8-16 K rows). */
 size_t silcu_sgemv_workspace_bytes(uint32_t N, uint32_t K);
 silcu_status silcu_sgemv(const float *x, const float *W, float *y, const float *bias, uint32_t N,
                          uint32_t K, void *workspace, size_t workspace_bytes, silcu_stream stream);
