@@ -254,6 +254,10 @@ typedef struct silcu_attention_args {
   int64_t ldv, sv_b, sv_h;
   int64_t ldo, so_b, so_h;
   float scale;
+  /* Alternatively V itself, [Sk, D] rows (split hi/lo), e.g. the V columns of
+   * a fused QKV projection read in place: set V_hi/V_lo and leave Vt_hi/Vt_lo
+   * NULL; ldv, sv_b, sv_h then describe V's rows.  (ABI version 2.) */
+  const float *V_hi, *V_lo;
 } silcu_attention_args;
 silcu_status silcu_attention_f32(const silcu_attention_args *args_host, silcu_stream stream);
 

@@ -61,7 +61,7 @@ class AttnArgs(C.Structure):
                 ("ldk", i64), ("sk_b", i64), ("sk_h", i64),
                 ("ldv", i64), ("sv_b", i64), ("sv_h", i64),
                 ("ldo", i64), ("so_b", i64), ("so_h", i64),
-                ("scale", f32)]
+                ("scale", f32), ("V_hi", vp), ("V_lo", vp)]
 
 
 _SIGS = {

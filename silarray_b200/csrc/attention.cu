@@ -62,9 +62,26 @@ struct __align__(64) AttnParams {
   float *O, *O_hi, *O_lo;
   int64_t ldo, so_b, so_h;
   int Sq, Sk, heads, tiles_q;
+  int v_rows;  // V given as [Sk, D] rows (B operand of P.V read MN-major), else V^T [D, Sk]
   float scale;
   int *err;
 };
+
+// Descriptor of V [keys, dims] rows as the MN-major B operand of P.V (N =
+// dims, K = keys).  For a 32-bit type the MN-major operand must use the
+// 128-byte swizzle with 32-byte atoms (descriptor layout 1), which the TMA
+// writes with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B: rows of 32 dims (128 B),
+// groups of 4 key rows 512 B apart (SBO), the second 32-dim box K_ATOM bytes
+// on (LBO = 8 KB).  One MMA (8 keys) spans two groups: 1024 B per k-step.
+__device__ __forceinline__ uint64_t make_desc_mn(uint32_t addr) {
+  uint64_t d = 0;
+  d |= uint64_t((addr & 0x3FFFFu) >> 4);
+  d |= uint64_t((KB * 128) >> 4) << 16;
+  d |= uint64_t(512 >> 4) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(1) << 61;
+  return d;
+}
 
 enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kSEmpty = 11, kPFull = 13,
            kPEmpty = 15, kOFull = 17, kOEmpty = 19, kNumBars = 21 };
@@ -162,8 +179,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
         const uint32_t dst = base + OFF_V + st * V_BYTES;
         mbar_expect_tx(bar(kVFull + st), V_BYTES);
         for (int a = 0; a < 2; a++) {
-          tma_load_4d(dst + a * K_ATOM, &p.v_hi, bar(kVFull + st), j * KB + 32 * a, 0, h, b);
-          tma_load_4d(dst + 2 * K_ATOM + a * K_ATOM, &p.v_lo, bar(kVFull + st), j * KB + 32 * a, 0, h, b);
+          if (p.v_rows) {  // V rows: the boxes of K (32 dims x 64 keys), 32-byte-atom swizzle
+            tma_load_4d(dst + a * K_ATOM, &p.v_hi, bar(kVFull + st), 32 * a, j * KB, h, b);
+            tma_load_4d(dst + 2 * K_ATOM + a * K_ATOM, &p.v_lo, bar(kVFull + st), 32 * a, j * KB, h, b);
+          } else {
+            tma_load_4d(dst + a * K_ATOM, &p.v_hi, bar(kVFull + st), j * KB + 32 * a, 0, h, b);
+            tma_load_4d(dst + 2 * K_ATOM + a * K_ATOM, &p.v_lo, bar(kVFull + st), j * KB + 32 * a, 0, h, b);
+          }
         }
       };
       load_k(0);
@@ -187,6 +209,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
       // descriptor, address / 16, so desc(a + o) = desc(a) + o / 16).
       const uint64_t dq = make_desc(base + OFF_Q);
       const uint64_t dk0 = make_desc(base + OFF_K), dv0 = make_desc(base + OFF_V);
+      const uint64_t dvm = make_desc_mn(base + OFF_V);
       bool ok = mbar_wait(bar(kQFull), 0, p.err, 13);
       auto pv = [&](int i) {
         const int u = i & 1;
@@ -195,15 +218,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
         if (i >= 2 && !mbar_wait(bar(kOEmpty + u), ((i >> 1) & 1) ^ 1, p.err, 16)) return false;
         tc_fence_after();
         const uint32_t pcol = tmem + COL_P + 128 * u;
-        const uint64_t dv = dv0 + uint64_t((u * V_BYTES) >> 4);
+        const bool mn = p.v_rows != 0;
+        const uint64_t dv = (mn ? dvm : dv0) + uint64_t((u * V_BYTES) >> 4);
+        const uint32_t idesc_pv = mn ? (IDESC | (1u << 16)) : IDESC;  // B MN-major for V rows
 #pragma unroll
         for (int kk = 0; kk < KB / 8; kk++) {
-          const uint64_t vh = dv + uint64_t(((kk >> 2) * K_ATOM + (kk & 3) * 32) >> 4);
+          // V^T: K-major, 8 keys = 32 bytes along a row; V rows: 8 keys = one 1024-byte row group.
+          const uint64_t vh = dv + uint64_t((mn ? kk * 1024 : (kk >> 2) * K_ATOM + (kk & 3) * 32) >> 4);
           const uint64_t vl = vh + uint64_t((2 * K_ATOM) >> 4);
           const uint32_t ph = pcol + 8 * kk, pl = pcol + 64 + 8 * kk;
-          mma_tf32_ts(tmem + COL_O + 64 * u, pl, vh, IDESC, kk == 0 ? 0u : 1u);
-          mma_tf32_ts(tmem + COL_O + 64 * u, ph, vl, IDESC, 1u);
-          mma_tf32_ts(tmem + COL_O + 64 * u, ph, vh, IDESC, 1u);
+          mma_tf32_ts(tmem + COL_O + 64 * u, pl, vh, idesc_pv, kk == 0 ? 0u : 1u);
+          mma_tf32_ts(tmem + COL_O + 64 * u, ph, vl, idesc_pv, 1u);
+          mma_tf32_ts(tmem + COL_O + 64 * u, ph, vh, idesc_pv, 1u);
         }
         mma_commit(bar(kVEmpty + u));
         mma_commit(bar(kPEmpty + u));
@@ -382,9 +408,12 @@ extern "C" silcu_status silcu_attention_f32(const silcu_attention_args *ap, silc
   if (a.D != HD) return fail(SILCU_UNSUPPORTED, "attention: head dimension %lld (only 64)", (long long)a.D);
   if (a.Sq <= 0 || a.Sk <= 0 || a.batch <= 0 || a.heads <= 0)
     return fail(SILCU_INVALID_ARGUMENT, "attention: empty extent");
+  const bool v_rows = a.V_hi || a.V_lo;
+  if (v_rows && (a.Vt_hi || a.Vt_lo)) return fail(SILCU_INVALID_ARGUMENT, "attention: give V or V^T, not both");
+  const float *v_hi = v_rows ? a.V_hi : a.Vt_hi, *v_lo = v_rows ? a.V_lo : a.Vt_lo;
   if (!(view_ok(a.Q_hi, a.ldq, a.sq_b, a.sq_h) && view_ok(a.Q_lo, a.ldq, a.sq_b, a.sq_h) &&
         view_ok(a.K_hi, a.ldk, a.sk_b, a.sk_h) && view_ok(a.K_lo, a.ldk, a.sk_b, a.sk_h) &&
-        view_ok(a.Vt_hi, a.ldv, a.sv_b, a.sv_h) && view_ok(a.Vt_lo, a.ldv, a.sv_b, a.sv_h)))
+        view_ok(v_hi, a.ldv, a.sv_b, a.sv_h) && view_ok(v_lo, a.ldv, a.sv_b, a.sv_h)))
     return fail(SILCU_INVALID_ARGUMENT, "attention: operands need 16-byte aligned rows and strides");
   const bool split_out = a.O_hi && a.O_lo;
   if (!a.O && !split_out) return fail(SILCU_INVALID_ARGUMENT, "attention: no output");
@@ -396,13 +425,17 @@ extern "C" silcu_status silcu_attention_f32(const silcu_attention_args *ap, silc
     return fail(SILCU_UNSUPPORTED, "attention: too large");
   AttnParams p;
   memset(&p, 0, sizeof(p));
+  const CUtensorMapSwizzle vsw = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;  // V rows: see make_desc_mn
   if (!make_map4(&p.q_hi, a.Q_hi, HD, a.Sq, a.ldq, a.heads, a.sq_h, a.batch, a.sq_b, 32, QT) ||
       !make_map4(&p.q_lo, a.Q_lo, HD, a.Sq, a.ldq, a.heads, a.sq_h, a.batch, a.sq_b, 32, QT) ||
       !make_map4(&p.k_hi, a.K_hi, HD, a.Sk, a.ldk, a.heads, a.sk_h, a.batch, a.sk_b, 32, KB) ||
       !make_map4(&p.k_lo, a.K_lo, HD, a.Sk, a.ldk, a.heads, a.sk_h, a.batch, a.sk_b, 32, KB) ||
-      !make_map4(&p.v_hi, a.Vt_hi, a.Sk, HD, a.ldv, a.heads, a.sv_h, a.batch, a.sv_b, 32, HD) ||
-      !make_map4(&p.v_lo, a.Vt_lo, a.Sk, HD, a.ldv, a.heads, a.sv_h, a.batch, a.sv_b, 32, HD))
+      !(v_rows ? make_map4(&p.v_hi, v_hi, HD, a.Sk, a.ldv, a.heads, a.sv_h, a.batch, a.sv_b, 32, KB, vsw)
+              : make_map4(&p.v_hi, v_hi, a.Sk, HD, a.ldv, a.heads, a.sv_h, a.batch, a.sv_b, 32, HD)) ||
+      !(v_rows ? make_map4(&p.v_lo, v_lo, HD, a.Sk, a.ldv, a.heads, a.sv_h, a.batch, a.sv_b, 32, KB, vsw)
+              : make_map4(&p.v_lo, v_lo, a.Sk, HD, a.ldv, a.heads, a.sv_h, a.batch, a.sv_b, 32, HD)))
     return fail(SILCU_CUDA_ERROR, "attention: cuTensorMapEncodeTiled failed");
+  p.v_rows = v_rows ? 1 : 0;
   p.O = a.O;
   p.O_hi = split_out ? a.O_hi : nullptr;
   p.O_lo = split_out ? a.O_lo : nullptr;

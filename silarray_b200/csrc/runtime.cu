@@ -60,7 +60,7 @@ extern "C" {
 
 const char *silcu_last_error(void) { return silcu::g_last_error; }
 
-int silcu_abi_version(void) { return 1; }
+int silcu_abi_version(void) { return 2; }
 
 unsigned long long silcu_kernel_launches(void) {
   return __atomic_load_n(&silcu::g_launches, __ATOMIC_RELAXED);

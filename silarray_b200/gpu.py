@@ -272,10 +272,15 @@ def transpose_split(src, rows, cols, ld, batch=1, heads=1, s_b=0, s_h=0, src_lo=
 
 
 def attention(Q, K, Vt, *, Sq, Sk, batch, heads, ldq, sq_b, sq_h, ldk, sk_b, sk_h, ldv, sv_b, sv_h,
-              scale, O=None, O_split=None, ldo=None, so_b=None, so_h=None, D=64):
-    """Fused softmax(Q.K^T * scale).V; Q, K, Vt are (hi, lo) split pairs."""
+              scale, O=None, O_split=None, ldo=None, so_b=None, so_h=None, D=64, V=None):
+    """Fused softmax(Q.K^T * scale).V; Q, K and Vt (V^T [D, Sk] rows) are
+    (hi, lo) split pairs.  Or pass Vt=None and V, V's [Sk, D] rows (e.g. the
+    V columns of a QKV projection in place); ldv / sv_b / sv_h then describe
+    V's rows."""
     a = _lib.AttnArgs()
-    for nm, pair in (("Q", Q), ("K", K), ("Vt", Vt)):
+    if (Vt is None) == (V is None):
+        raise ValueError("attention: give exactly one of Vt and V")
+    for nm, pair in (("Q", Q), ("K", K), ("Vt", Vt) if Vt is not None else ("V", V)):
         _dev(pair[0], _F32), _dev(pair[1], _F32)
         setattr(a, nm + "_hi", pair[0].data_ptr())
         setattr(a, nm + "_lo", pair[1].data_ptr())

@@ -90,9 +90,10 @@ class Block:
 
     Operands of the tensor-core GEMMs travel as exact tf32 splits (hi, lo):
     the weights are split (and transposed to K-major) once here; in the
-    forward, layer_norm, softmax and the GEMM epilogues write their results
-    already split, so no GEMM re-reads an operand just to split it (V, read
-    N-major by the context GEMM, is the one operand re-split per forward)."""
+    forward, layer_norm, attention and the GEMM epilogues write their results
+    already split, so no kernel re-reads an operand just to split it;
+    attention reads Q, K and V in place from the QKV output (V as the MN-major
+    operand of its P.V product)."""
 
     def __init__(self, cfg, params, device="cuda"):
         self.cfg = cfg
@@ -113,7 +114,6 @@ class Block:
         pair = lambda n: (e(n), e(n))  # noqa: E731
         self.h = pair(T * d)
         self.qkv = pair(T * 3 * d)
-        self.vt = pair(cfg.batch * H * cfg.head_dim * S)
         self.ctx = pair(T * d)
         self.r1 = e(T * d)
         self.ff = pair(T * f)
@@ -240,18 +240,14 @@ class Block:
         xs, outs = x[t0 * d:(t0 + T) * d], out[t0 * d:(t0 + T) * d]
         h, qkv, ctx, ff = rows(self.h, d), rows(self.qkv, 3 * d), rows(self.ctx, d), rows(self.ff, f)
         r1 = self.r1[t0 * d:(t0 + T) * d]
-        vo = b0 * H * hd * S
-        vt = (self.vt[0][vo:vo + nb * H * hd * S], self.vt[1][vo:vo + nb * H * hd * S])
         qh, ql = qkv
         gpu.layer_norm_split(xs, self.g1, self.be1, T, d, cfg.eps, *h)
         gpu.gemm(h, self.wqkv_t, M=T, N=3 * d, K=d, trans_b=True, bias=self.bqkv, no_c=True, C_split=qkv)
         # ctx[b*S + s, h*hd + j] = softmax(Q_bh . K_bh^T * scale) . V_bh, fused; Q_bh rows are
-        # qkv[b*S + s, h*hd : h*hd + hd], K_bh the same at +d; V_bh^T comes split and transposed.
-        gpu.transpose_split(qh[2 * d:], S, hd, 3 * d, batch=nb, heads=H, s_b=S * 3 * d, s_h=hd,
-                            src_lo=ql[2 * d:], out=vt)
-        gpu.attention((qh, ql), (qh[d:], ql[d:]), vt, Sq=S, Sk=S, batch=nb, heads=H,
-                      ldq=3 * d, sq_b=S * 3 * d, sq_h=hd, ldk=3 * d, sk_b=S * 3 * d, sk_h=hd,
-                      ldv=S, sv_b=H * hd * S, sv_h=hd * S, scale=self.scale,
+        # qkv[b*S + s, h*hd : h*hd + hd], K_bh the same at +d, V_bh at +2d: all read in place.
+        gpu.attention((qh, ql), (qh[d:], ql[d:]), None, V=(qh[2 * d:], ql[2 * d:]), Sq=S, Sk=S, batch=nb,
+                      heads=H, ldq=3 * d, sq_b=S * 3 * d, sq_h=hd, ldk=3 * d, sk_b=S * 3 * d, sk_h=hd,
+                      ldv=3 * d, sv_b=S * 3 * d, sv_h=hd, scale=self.scale,
                       O_split=ctx, ldo=d, so_b=S * d, so_h=hd)
         gpu.gemm(ctx, self.wo_t, r1, M=T, N=d, K=d, trans_b=True, bias=self.bo, residual=xs)
         gpu.layer_norm_split(r1, self.g2, self.be2, T, d, cfg.eps, *h)

@@ -22,7 +22,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_abi_version(lib):
-    assert lib.silcu_abi_version() == 1
+    assert lib.silcu_abi_version() == 2
 
 
 def test_null_pointers_are_rejected_with_status(lib):

@@ -42,3 +42,30 @@ def test_attention_matches_chain(cuda, B, H, S):
             assert_dot_close(got[b, h], _ref(q[b, h], k[b, h], v[b, h], np.float32(scale)), S,
                              what=f"attention b{b} h{h}")
     gpu.device_status()
+
+
+@pytest.mark.parametrize("B,H,S", [(1, 1, 64), (2, 3, 200), (1, 2, 300), (1, 1, 1000)])
+def test_attention_v_rows(cuda, B, H, S):
+    """V given as its [Sk, D] rows (read in place, e.g. from a QKV projection)
+    instead of V^T: the same products in the same order, so the output equals
+    the V^T form bit for bit, and the oracle chain within tolerance."""
+    D = 64
+    rng = np.random.default_rng(S * 3 + H)
+    q = rng.normal(0, 1, (B, H, S, D)).astype(np.float32)
+    k = rng.normal(0, 1, (B, H, S, D)).astype(np.float32)
+    v = rng.normal(0, 1, (B, H, S, D)).astype(np.float32)
+    dq, dk, dv = (torch.from_numpy(t).cuda().reshape(-1) for t in (q, k, v))
+    qs, ks, vs = (gpu.split(t, B * H * S, D) for t in (dq, dk, dv))
+    vt = gpu.transpose_split(dv, S, D, D, batch=B, heads=H, s_b=H * S * D, s_h=S * D)
+    common = dict(Sq=S, Sk=S, batch=B, heads=H, ldq=D, sq_b=H * S * D, sq_h=S * D, ldk=D, sk_b=H * S * D,
+                  sk_h=S * D, scale=float(np.float32(0.125)))
+    o_t = gpu.attention(qs, ks, vt, ldv=S, sv_b=H * D * S, sv_h=D * S, **common)
+    o_r = gpu.attention(qs, ks, None, V=vs, ldv=D, sv_b=H * S * D, sv_h=S * D, **common)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(o_r.cpu().numpy(), o_t.cpu().numpy())
+    got = o_r.cpu().numpy().reshape(B, H, S, D)
+    for b in range(B):
+        for h in range(H):
+            assert_dot_close(got[b, h], _ref(q[b, h], k[b, h], v[b, h], np.float32(0.125)), S,
+                             what=f"attention (V rows) b{b} h{h}")
+    gpu.device_status()
