@@ -92,10 +92,14 @@ struct __align__(64) TcParams {
   CUtensorMap a_hi, a_lo, b_hi, b_lo;  // 4-D {K, rows, batch_inner, batch}, box {32, 128|BN, 1, 1}
   CUtensorMap c_map, chi_map, clo_map; // 4-D {N, M, batch_inner, batch}, box {32, 32, 1, 1}
   CUtensorMap r_map;                   // the residual, same layout as C (used when tma_r)
+  CUtensorMap p_map;                   // split-K partials: 4-D {BN, TM, ksplit, split tiles}, box {32, 32, 1, 1}
   float *C;                            // direct-store fallback when C cannot take TMA stores
   int64_t ldc, stride_c, stride_c_in;
   int M, N, K, tiles_m, tiles_n, nbatch, bin, chunk_kb;
-  int ksplit;  // > 1: each tile's K range in ksplit parts, partials stored through c_map at z = part
+  // Work items: tiles [0, full_items) whole; each later tile's K range in
+  // ksplit parts whose plain partials leave through p_map (the epilogue then
+  // runs in tile_finish).  full_items = all tiles when nothing is split.
+  int full_items, ksplit;
   int tma_c, split_out, tma_r;
   TcEpi epi;
   int *err;
@@ -107,20 +111,24 @@ struct Tile {
 
 // Grouped raster inside one batch: GROUP_M tile-rows sweep the N tiles
 // together so the A and B strips they share stay in L2.
-template <int TM, int BN>
-__device__ __forceinline__ Tile decode_tile(const TcParams &p, int idx) {
-  const int tiles_per_batch = p.tiles_m * p.tiles_n;
+__host__ __device__ __forceinline__ Tile tile_at(int tiles_m, int tiles_n, int TM, int BN, int idx) {
+  const int tiles_per_batch = tiles_m * tiles_n;
   Tile r;
   r.bz = idx / tiles_per_batch;
   const int t = idx % tiles_per_batch;
-  const int group = t / (GROUP_M * p.tiles_n);
+  const int group = t / (GROUP_M * tiles_n);
   const int first_m = group * GROUP_M;
-  const int gm = min(p.tiles_m - first_m, GROUP_M);
-  const int tm = first_m + (t % (GROUP_M * p.tiles_n)) % gm;
-  const int tn = (t % (GROUP_M * p.tiles_n)) / gm;
+  const int gm = tiles_m - first_m < GROUP_M ? tiles_m - first_m : GROUP_M;
+  const int tm = first_m + (t % (GROUP_M * tiles_n)) % gm;
+  const int tn = (t % (GROUP_M * tiles_n)) / gm;
   r.m0 = tm * TM;
   r.n0 = tn * BN;
   return r;
+}
+
+template <int TM, int BN>
+__device__ __forceinline__ Tile decode_tile(const TcParams &p, int idx) {
+  return tile_at(p.tiles_m, p.tiles_n, TM, BN, idx);
 }
 
 
@@ -176,18 +184,20 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
   const uint32_t tfull0 = smem_u32(bars + 2 * STAGES), tempty0 = smem_u32(bars + 2 * STAGES + NBUF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Work items: (tile, K part); ksplit = 1 unless the tiles alone would leave SMs idle.
-  const int total_tiles = p.tiles_m * p.tiles_n * p.nbatch * p.ksplit;
+  // Work items: whole tiles, then (tile, K part) for the split tiles.
+  const int total_tiles = p.full_items + (p.tiles_m * p.tiles_n * p.nbatch - p.full_items) * p.ksplit;
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
   const int first_tile = PAIR ? int(blockIdx.x >> 1) : int(blockIdx.x);
   const int tile_step = PAIR ? int(gridDim.x >> 1) : int(gridDim.x);
   const int nk = (p.K + BK - 1) / BK;
   const int CHUNK_KB = p.chunk_kb;
   // K blocks [kb0, kb1) of a work item, and its number of accumulation chunks.
+  auto item_tile = [&](int item) { return item < p.full_items ? item : p.full_items + (item - p.full_items) / p.ksplit; };
+  auto item_part = [&](int item) { return item < p.full_items ? -1 : (item - p.full_items) % p.ksplit; };
   auto k_range = [&](int item, int &kb0, int &kb1) {
-    const int ks = item % p.ksplit;
-    kb0 = ks * nk / p.ksplit;
-    kb1 = (ks + 1) * nk / p.ksplit;
+    const int ks = item_part(item);
+    kb0 = ks < 0 ? 0 : ks * nk / p.ksplit;
+    kb1 = ks < 0 ? nk : (ks + 1) * nk / p.ksplit;
   };
 
   if (threadIdx.x == 0) {
@@ -224,7 +234,7 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
       uint32_t kbg = 0;
       bool ok = true;
       for (int tile = first_tile; tile < total_tiles && ok; tile += tile_step) {
-        const Tile tl = decode_tile<C::TM, BN>(p, tile / p.ksplit);
+        const Tile tl = decode_tile<C::TM, BN>(p, item_tile(tile));
         const int bo = tl.bz / p.bin, bi = tl.bz % p.bin;
         const int am = tl.m0 + BM * int(rank), bn = tl.n0 + C::ROWS_B * int(rank);
         int kbs, kbe;
@@ -319,7 +329,7 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
     uint32_t cg = 0;
     bool ok = true;
     for (int tile = first_tile; tile < total_tiles && ok; tile += tile_step) {
-      const Tile tl = decode_tile<C::TM, BN>(p, tile / p.ksplit);
+      const Tile tl = decode_tile<C::TM, BN>(p, item_tile(tile));
       const int m0 = tl.m0 + BM * int(rank);  // this CTA's 128 rows of the tile
       int kbs, kbe;
       k_range(tile, kbs, kbe);
@@ -356,10 +366,36 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
       }
       const bool good = __all_sync(0xffffffffu, ok && *reinterpret_cast<volatile int *>(p.err) == 0);
       if (!good) break;
+      const int part = item_part(tile);
+      if (part >= 0) {
+        // A K part of a split tile: its plain partial, no epilogue.
+        if (m0 + 32 * q >= p.M) continue;
+#pragma unroll
+        for (int cb = 0; cb < EC / 32; cb++) {
+          const int col0 = tl.n0 + h * EC + 32 * cb;
+          if (col0 >= p.N) break;  // warp-uniform
+          float *sb = st + (C::OUT_BUFS == 2 ? (nstore & 1) * 1024 : 0);
+          if (lane == 0) {
+            if (C::OUT_BUFS == 2) bulk_wait_read1();
+            else bulk_wait_read0();
+          }
+          __syncwarp();
+          stage_row_swz(sb, lane, acc, 32 * cb, 0);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_4d(&p.p_map, smem_u32(sb), h * EC + 32 * cb, BM * int(rank) + 32 * q, part,
+                         item_tile(tile) - p.full_items);
+            bulk_commit();
+          }
+          nstore++;
+        }
+        continue;
+      }
       // Epilogue math in registers (lane = row): alpha, bias, activation,
       // residual, in the reference's order; then 32x32 blocks leave through
       // shared memory (TMA stores, or a transposed coalesced store fallback).
-      const int bo = tl.bz / p.bin, bi = p.ksplit > 1 ? tile % p.ksplit : tl.bz % p.bin;
+      const int bo = tl.bz / p.bin, bi = tl.bz % p.bin;
       const int row = m0 + 32 * q + lane;
       const int64_t coff = int64_t(bo) * p.stride_c + int64_t(bi) * p.stride_c_in;
 #pragma unroll
@@ -686,14 +722,20 @@ struct TcPlan {
   bool pair;
   int BN, TM, ksplit;
   int64_t tiles_m, tiles_n;
+  int64_t full_items;  // tiles run whole; the rest run in ksplit K parts
 };
 
-// CTA pairs and tile width as above; split K when the tiles alone would fill
-// less than 60 % of the grid (small M with N = 768, e.g. a shard of the
-// transformer batch on 8 GPUs): up to 8 parts of at least four accumulation
-// chunks (512 k) each, batch 1 only.  Measured at M = 2048, N = 768: K = 3072
-// 111 -> 85 us in 3 parts; K = 768 would lose (37 -> 42 us), so it does not
-// split.  SILCU_TC_KSPLIT = 1 disables it, 2..8 forces the parts (tuning).
+// CTA pairs and tile width as above; then split K (batch 1 only) where the
+// tiles leave SMs idle:
+//  - all tiles, when they alone would fill less than 60 % of the grid (small
+//    M with N = 768, e.g. a shard of the transformer batch on 8 GPUs): up to
+//    8 parts;
+//  - otherwise only the tiles of a last, partial wave, in as many parts as
+//    keep that wave within the grid (e.g. M = 2048, N = 3072: 96 pair tiles
+//    on 74 pairs run as 74 whole tiles plus 22 tiles in 3 parts).
+// Every part keeps at least two accumulation chunks (256 k).
+// SILCU_TC_KSPLIT = 1 disables splitting, 2..8 splits every tile in that
+// many parts; SILCU_TC_TAIL = 0 disables the last-wave split (tuning).
 TcPlan tc_plan(const silcu_gemm_args &a) {
   TcPlan pl;
   const int64_t Kp = padded_k(a.K > 0 ? a.K : 1);
@@ -708,44 +750,115 @@ TcPlan tc_plan(const silcu_gemm_args &a) {
     const char *e = getenv("SILCU_TC_KSPLIT");
     return e ? atoi(e) : 0;
   }();
+  static const bool tail = [] {
+    const char *e = getenv("SILCU_TC_TAIL");
+    return !(e && atoi(e) == 0);
+  }();
   const int64_t units = pl.pair ? sm_count() / 2 : sm_count();
   const int64_t tiles = pl.tiles_m * pl.tiles_n * nb;
+  pl.full_items = tiles;
   const int64_t nkb = (Kp + BK - 1) / BK;
-  if (nb == 1 && forced != 1 && tiles * 10 < units * 6 && a.N % 4 == 0) {
-    int ks = int(units / tiles);
-    if (forced >= 2 && forced <= 8) ks = forced;
+  if (nb != 1 || forced == 1) return pl;
+  auto parts = [&](int64_t ks) {
     if (ks > 8) ks = 8;
-    while (ks > 1 && nkb / ks < 4 * CHUNK_KB_DEFAULT) ks--;  // short parts lose to the extra pass
-    pl.ksplit = ks;
+    while (ks > 1 && nkb / ks < 2 * CHUNK_KB_DEFAULT) ks--;  // short parts lose to the extra pass
+    return int(ks);
+  };
+  if (forced >= 2 && forced <= 8) {
+    pl.ksplit = int(forced < nkb ? forced : nkb);
+    pl.full_items = 0;
+  } else if (tiles * 10 < units * 6) {
+    pl.ksplit = parts(units / tiles);
+    pl.full_items = pl.ksplit > 1 ? 0 : tiles;
+  } else if (tail && tiles > units && tiles % units != 0) {
+    const int64_t rem = tiles % units;
+    pl.ksplit = parts(units / rem);
+    pl.full_items = pl.ksplit > 1 ? tiles - rem : tiles;
   }
   return pl;
 }
 
 size_t partial_bytes(const silcu_gemm_args &a, const TcPlan &pl) {
-  return pl.ksplit > 1 ? size_t(pl.ksplit) * size_t(a.M) * size_t(a.N) * sizeof(float) + 256 : 0;
+  const int64_t tiles = pl.tiles_m * pl.tiles_n * total_batch(a);
+  return pl.ksplit > 1 ? size_t(tiles - pl.full_items) * pl.ksplit * pl.TM * pl.BN * sizeof(float) + 256 : 0;
 }
 
-// Sum of the split-K partials in part order (round to nearest), then the
-// epilogue in the tensor-core kernel's order: alpha, bias, activation,
-// residual; plain and / or split (hi, lo) output.
-__global__ void __launch_bounds__(256) splitk_finish(const float *__restrict__ part, int ksplit, int64_t M, int64_t N,
-                                                     TcEpi epi, float *C, int64_t ldc, float *C_hi, float *C_lo) {
-  const int64_t total = M * N;
-  for (int64_t j = int64_t(blockIdx.x) * 256 + threadIdx.x; j < total; j += int64_t(gridDim.x) * 256) {
-    const int64_t row = j / N, col = j % N;
-    float v = part[j];
-    for (int k = 1; k < ksplit; k++) v = __fadd_rn(v, part[int64_t(k) * total + j]);
-    if (epi.alpha != 1.0f) v = __fmul_rn(v, epi.alpha);
-    if (epi.bias) v = __fadd_rn(v, epi.bias[col % epi.bias_len]);
-    if (epi.act == SILCU_ACT_RELU) v = v >= 0.0f ? v : 0.0f;
-    else if (epi.act == SILCU_ACT_SIGMOID) v = sigmoid_ref(v);
-    if (epi.residual) v = __fadd_rn(v, epi.residual[row * epi.ldr + col]);
-    const int64_t o = row * ldc + col;
-    if (C) C[o] = v;
+// Finishes the split tiles: sums each element's K-part partials in part
+// order (round to nearest), then the epilogue in the tensor-core kernel's
+// order: alpha, bias, activation, residual; plain and / or split (hi, lo)
+// output.  blockIdx.y = split tile, a thread = 4 columns of one row; vec
+// (N, ldc, ldr multiples of 4 and 16-byte aligned outputs / residual) selects
+// 16-byte accesses.
+__device__ __forceinline__ float finish_one(float v, int64_t col, const TcEpi &epi) {
+  if (epi.alpha != 1.0f) v = __fmul_rn(v, epi.alpha);
+  if (epi.bias) v = __fadd_rn(v, epi.bias[col % epi.bias_len]);
+  if (epi.act == SILCU_ACT_RELU) v = v >= 0.0f ? v : 0.0f;
+  else if (epi.act == SILCU_ACT_SIGMOID) v = sigmoid_ref(v);
+  return v;
+}
+
+__global__ void __launch_bounds__(256) tile_finish(const float *__restrict__ part, int ksplit, int full_items,
+                                                   int tiles_m, int tiles_n, int TM, int BN, int M, int N,
+                                                   TcEpi epi, float *C, int64_t ldc, float *C_hi, float *C_lo,
+                                                   int vec) {
+  const int bn4 = BN >> 2;
+  const int g = blockIdx.x * 256 + threadIdx.x;
+  if (g >= TM * bn4) return;
+  const int rin = g / bn4, cin = (g - rin * bn4) << 2;
+  const Tile tl = tile_at(tiles_m, tiles_n, TM, BN, full_items + int(blockIdx.y));
+  const int row = tl.m0 + rin, col = tl.n0 + cin;
+  if (row >= M || col >= N) return;
+  const int64_t plane = int64_t(TM) * BN;
+  const float *src = part + int64_t(blockIdx.y) * ksplit * plane + int64_t(rin) * BN + cin;
+  float4 q[8];
+#pragma unroll
+  for (int k = 0; k < 8; k++)
+    if (k < ksplit) q[k] = __ldcs(reinterpret_cast<const float4 *>(src + k * plane));
+  float v[4] = {q[0].x, q[0].y, q[0].z, q[0].w};
+#pragma unroll
+  for (int k = 1; k < 8; k++)
+    if (k < ksplit) {
+      v[0] = __fadd_rn(v[0], q[k].x);
+      v[1] = __fadd_rn(v[1], q[k].y);
+      v[2] = __fadd_rn(v[2], q[k].z);
+      v[3] = __fadd_rn(v[3], q[k].w);
+    }
+  const int nv = N - col < 4 ? N - col : 4;
+  float rr[4] = {0.f, 0.f, 0.f, 0.f};
+  if (epi.residual) {
+    const float *rp = epi.residual + int64_t(row) * epi.ldr + col;
+    if (vec) {
+      const float4 r = __ldg(reinterpret_cast<const float4 *>(rp));
+      rr[0] = r.x, rr[1] = r.y, rr[2] = r.z, rr[3] = r.w;
+    } else {
+      for (int i = 0; i < nv; i++) rr[i] = __ldg(rp + i);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    v[i] = finish_one(v[i], int64_t(col) + i, epi);
+    if (epi.residual) v[i] = __fadd_rn(v[i], rr[i]);
+  }
+  const int64_t o = int64_t(row) * ldc + col;
+  float h[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    h[i] = tf32_rna(v[i]);
+    l[i] = __fsub_rn(v[i], h[i]);
+  }
+  if (vec) {
+    if (C) *reinterpret_cast<float4 *>(C + o) = make_float4(v[0], v[1], v[2], v[3]);
     if (C_hi) {
-      const float hi = tf32_rna(v);
-      C_hi[o] = hi;
-      C_lo[o] = __fsub_rn(v, hi);
+      *reinterpret_cast<float4 *>(C_hi + o) = make_float4(h[0], h[1], h[2], h[3]);
+      *reinterpret_cast<float4 *>(C_lo + o) = make_float4(l[0], l[1], l[2], l[3]);
+    }
+  } else {
+    for (int i = 0; i < nv; i++) {
+      if (C) C[o + i] = v[i];
+      if (C_hi) {
+        C_hi[o + i] = h[i];
+        C_lo[o + i] = l[i];
+      }
     }
   }
 }
@@ -881,20 +994,17 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
   p.err = device_error_ptr();
   if (!p.err) return fail(SILCU_CUDA_ERROR, "sgemm(tc): no device error word");
   p.ksplit = plan.ksplit;
+  p.full_items = int(plan.full_items);
+  const int64_t split_tiles = tiles_m * tiles_n * nb - plan.full_items;
   float *part = nullptr;
   if (plan.ksplit > 1) {
-    // The kernel stores plain partials (part k at z = k); the epilogue runs in splitk_finish.
+    // Split tiles store plain partials (tile t, part k at z = k, w = t); their epilogue runs in tile_finish.
     part = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(cur) + 255) & ~uintptr_t(255));
-    if (!make_map4(&p.c_map, part, a.N, a.M, a.N, plan.ksplit, a.M * a.N, 1, plan.ksplit * a.M * a.N, 32, 32))
+    const int64_t plane = int64_t(plan.TM) * BN;
+    if (!make_map4(&p.p_map, part, BN, plan.TM, BN, plan.ksplit, plane, split_tiles, plan.ksplit * plane, 32, 32))
       return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed (split-K partials)");
-    p.tma_c = 1;
-    p.split_out = 0;
-    p.epi.alpha = 1.0f;
-    p.epi.bias = nullptr;
-    p.epi.act = SILCU_ACT_NONE;
-    p.epi.residual = nullptr;
   }
-  const int64_t total = tiles_m * tiles_n * nb * plan.ksplit;
+  const int64_t total = plan.full_items + split_tiles * plan.ksplit;
   silcu_status st;
   if (pair) {
     const int64_t pairs = sm_count() / 2;
@@ -916,11 +1026,14 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
   epi.act = a.act;
   epi.residual = a.residual;
   epi.ldr = a.ldr;
-  const int64_t n = a.M * a.N;
-  const int64_t blocks = (n + 255) / 256, cap = int64_t(sm_count()) * 8;
-  splitk_finish<<<uint32_t(blocks < cap ? blocks : cap), 256, 0, s>>>(part, plan.ksplit, a.M, a.N, epi, a.C, a.ldc,
-                                                                     split_out ? a.C_hi : nullptr,
-                                                                     split_out ? a.C_lo : nullptr);
+  float *c_hi = split_out ? a.C_hi : nullptr, *c_lo = split_out ? a.C_lo : nullptr;
+  auto al16 = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  const int vec = a.N % 4 == 0 && (!a.C || (a.ldc % 4 == 0 && al16(a.C))) &&
+                  (!c_hi || (a.ldc % 4 == 0 && al16(c_hi) && al16(c_lo))) &&
+                  (!a.residual || (a.ldr % 4 == 0 && al16(a.residual)));
+  const dim3 grid(uint32_t((plan.TM * BN / 4 + 255) / 256), uint32_t(split_tiles));
+  tile_finish<<<grid, 256, 0, s>>>(part, plan.ksplit, p.full_items, p.tiles_m, p.tiles_n, plan.TM, BN, p.M, p.N, epi,
+                                   a.C, a.ldc, c_hi, c_lo, vec);
   return check_launch("sgemm(tc) split-K finish");
 }
 
