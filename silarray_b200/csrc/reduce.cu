@@ -6,17 +6,20 @@
 // finish kernel combines the partials in index order, so results are
 // deterministic for a given GPU.
 //
-// Row ops keep the whole row on chip: each thread holds VPT float4 of the
-// row in registers, so softmax and layer_norm read HBM once and write once
-// (the reference reads the row 2-3 times: include/gpu_kernels.metal:1316-1467).
+// Row ops keep the whole row on chip (each thread's VPT float4 in registers,
+// or, for rows of 4K-32K columns, the row in shared memory by one bulk copy
+// per CTA), so softmax and layer_norm read HBM once and write once (the
+// reference reads the row 2-3 times: include/gpu_kernels.metal:1316-1467).
 #include <stdlib.h>
 #include <cooperative_groups.h>
 #include <float.h>
 
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace silcu {
 namespace {
+
 
 // ------------------------------------------------------------- block reduce
 template <int NT, typename T, typename F>
@@ -243,6 +246,7 @@ struct RowArgs {
   const float *gamma, *beta;
   uint32_t rows, cols;
   float eps;
+  int *err = nullptr;  // device error word of the bounded waits (TMA-staged kernel)
 };
 
 __device__ __forceinline__ float tf32_hi(float x) {
@@ -383,6 +387,147 @@ __global__ void __launch_bounds__(WARP ? 256 : NT) row_kernel(const RowArgs a) {
       if (t == 0) a.idx[row] = best ? int32_t(0xFFFFFFFFu - uint32_t(best & 0xFFFFFFFFu)) : 0;
     }
   }
+}
+
+// Long rows from shared memory: a cluster of CL CTAs per row (CL = 1: one
+// CTA), each CTA's column part brought in by one bulk copy (completing on an
+// mbarrier) and read from shared memory in every pass, so a CTA needs few
+// registers and an SM holds as many rows in flight as its shared memory
+// fits.  Softmax keeps exp(x - max) in place for the final scaling.
+template <int OP, int CL, int NT>
+__global__ void __launch_bounds__(NT) row_smem_kernel(const RowArgs a) {
+  extern __shared__ __align__(128) float4 rs[];  // cols / CL floats
+  __shared__ __align__(8) uint64_t full;
+  namespace cg = cooperative_groups;
+  __shared__ float sf[NT / 32];
+  __shared__ unsigned long long sk[NT / 32];
+  __shared__ float xf[2];
+  __shared__ unsigned long long xk;
+  const int t = threadIdx.x;
+  uint32_t rank = 0;
+  if constexpr (CL > 1) rank = cg::this_cluster().block_rank();
+  const uint32_t row = blockIdx.x / CL;
+  const uint32_t part = a.cols / 4 / CL;  // float4 per CTA
+  const uint32_t c0 = rank * part;
+  const uint32_t bar = tc::smem_u32(&full);
+  if (t == 0) {
+    tc::mbar_init(bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tc::mbar_expect_tx(bar, part * 16);
+    const float *src = a.in + size_t(row) * a.cols + size_t(c0) * 4;
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     tc::smem_u32(rs)),
+                 "l"(src), "r"(part * 16), "r"(bar)
+                 : "memory");
+  }
+  __syncthreads();
+  // A failed wait (error word set) computes on whatever is in shared memory;
+  // the host reads the status.  Every thread waits, so none reads early.
+  tc::mbar_wait(bar, 0, a.err, 41);
+  auto cl_combine = [&](float x, int slot, bool is_max) {
+    if constexpr (CL > 1) {
+      cg::cluster_group cl = cg::this_cluster();
+      if (t == 0) xf[slot] = x;
+      cl.sync();
+      float r = is_max ? __int_as_float(0xff800000) : 0.f;
+#pragma unroll
+      for (int q = 0; q < CL; q++) {
+        const float y = *cl.map_shared_rank(&xf[slot], q);
+        r = is_max ? fmaxf(r, y) : r + y;
+      }
+      return r;
+    }
+    return x;
+  };
+  if (OP == kSoftmax) {
+    float m = __int_as_float(0xff800000);
+    for (uint32_t c = t; c < part; c += NT) {
+      const float4 v = rs[c];
+      m = fmaxf(m, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+    }
+    m = cl_combine(block_reduce<NT>(m, sf, Max()), 0, true);
+    float s = 0.f;
+    for (uint32_t c = t; c < part; c += NT) {
+      float4 v = rs[c];
+      v.x = expf(__fsub_rn(v.x, m));
+      v.y = expf(__fsub_rn(v.y, m));
+      v.z = expf(__fsub_rn(v.z, m));
+      v.w = expf(__fsub_rn(v.w, m));
+      s += (v.x + v.y) + (v.z + v.w);
+      rs[c] = v;  // this thread's own element: no barrier needed before it is read back
+    }
+    s = cl_combine(block_reduce<NT>(s, sf, Add()), 1, false);
+    const float inv = __frcp_rn(s);
+    for (uint32_t c = t; c < part; c += NT) {
+      const float4 v = rs[c];
+      row_store4(a, row, c0 + c,
+                 make_float4(__fmul_rn(v.x, inv), __fmul_rn(v.y, inv), __fmul_rn(v.z, inv), __fmul_rn(v.w, inv)));
+    }
+  } else if (OP == kLayerNorm) {
+    float s = 0.f;
+    for (uint32_t c = t; c < part; c += NT) {
+      const float4 v = rs[c];
+      s += (v.x + v.y) + (v.z + v.w);
+    }
+    s = cl_combine(block_reduce<NT>(s, sf, Add()), 0, false);
+    const float mu = __fdiv_rn(s, float(a.cols));
+    float ss = 0.f;
+    for (uint32_t c = t; c < part; c += NT) {
+      const float4 v = rs[c];
+      const float dx = __fsub_rn(v.x, mu), dy = __fsub_rn(v.y, mu), dz = __fsub_rn(v.z, mu),
+                  dw = __fsub_rn(v.w, mu);
+      ss += (__fmul_rn(dx, dx) + __fmul_rn(dy, dy)) + (__fmul_rn(dz, dz) + __fmul_rn(dw, dw));
+    }
+    ss = cl_combine(block_reduce<NT>(ss, sf, Add()), 1, false);
+    const float inv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(a.cols)), a.eps)));
+    const float4 *g4 = reinterpret_cast<const float4 *>(a.gamma);
+    const float4 *b4 = reinterpret_cast<const float4 *>(a.beta);
+    for (uint32_t c = t; c < part; c += NT) {
+      const float4 v = rs[c];
+      const float4 g = __ldg(g4 + c0 + c), b = __ldg(b4 + c0 + c);
+      float4 o;
+      o.x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.x, mu), inv), g.x), b.x);
+      o.y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.y, mu), inv), g.y), b.y);
+      o.z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.z, mu), inv), g.z), b.z);
+      o.w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.w, mu), inv), g.w), b.w);
+      row_store4(a, row, c0 + c, o);
+    }
+  } else if (OP == kRowSum) {
+    float s = 0.f;
+    for (uint32_t c = t; c < part; c += NT) {
+      const float4 v = rs[c];
+      s += (v.x + v.y) + (v.z + v.w);
+    }
+    s = cl_combine(block_reduce<NT>(s, sf, Add()), 0, false);
+    if (rank == 0 && t == 0) a.out[row] = s;
+  } else {
+    float bv = FLT_MIN;
+    int32_t bi = -1;
+    for (uint32_t c = t; c < part; c += NT) {
+      const float4 v = rs[c];
+      const int32_t base = int32_t((c0 + c) * 4);
+      if (v.x > bv) { bv = v.x; bi = base; }
+      if (v.y > bv) { bv = v.y; bi = base + 1; }
+      if (v.z > bv) { bv = v.z; bi = base + 2; }
+      if (v.w > bv) { bv = v.w; bi = base + 3; }
+    }
+    unsigned long long best = bi >= 0 ? amax_key(bv, uint32_t(bi)) : 0ull;
+    best = block_reduce<NT>(best, sk, Max());
+    if constexpr (CL > 1) {
+      cg::cluster_group cl = cg::this_cluster();
+      if (t == 0) xk = best;
+      cl.sync();
+      if (rank == 0 && t == 0) {
+#pragma unroll
+        for (int q = 0; q < CL; q++) {
+          const unsigned long long k = *cl.map_shared_rank(&xk, q);
+          best = best > k ? best : k;
+        }
+      }
+    }
+    if (rank == 0 && t == 0) a.idx[row] = best ? int32_t(0xFFFFFFFFu - uint32_t(best & 0xFFFFFFFFu)) : 0;
+  }
+  if constexpr (CL > 1) cg::this_cluster().sync();  // peers may still be reading this CTA's exchange slots
 }
 
 // Long rows: a cluster of CL CTAs shares one row (each holds 1/CL of it in
@@ -612,6 +757,57 @@ cudaError_t launch_row_cluster(const RowArgs &a, cudaStream_t s) {
   return wide ? launch_cluster_cfg<OP, 8, 4, 256>(a, s) : launch_cluster_cfg<OP, 4, 4, 256>(a, s);
 }
 
+// One cluster (CTA) per row, the row part in dynamic shared memory.
+template <int OP, int CL, int NT>
+cudaError_t launch_smem(RowArgs a, cudaStream_t s) {
+  auto kern = row_smem_kernel<OP, CL, NT>;
+  a.err = device_error_ptr();
+  if (!a.err) return cudaErrorUnknown;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!configured[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.rows * CL);
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = size_t(a.cols / CL) * 4;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = CL;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+// Rows of 4K-32K columns (multiples of 64): softmax, layer_norm and argmax
+// from shared memory (measured at 4096 x 8192: 0.95 / 0.88 / 0.92 of HBM
+// against 0.93 / 0.79 / 0.89 with the row in registers; at 4096 x 32768
+// 0.70 / 0.69 / 0.76 against 0.69 / 0.64 / 0.76); the row sum from
+// registers (0.97 / 0.98 against 0.94 / 0.77).  SILCU_ROW_IMPL = 0 / 1
+// forces registers / shared memory (tuning).
+template <int OP>
+cudaError_t launch_row_long(const RowArgs &a, cudaStream_t s) {
+  static const int impl = [] {
+    const char *e = getenv("SILCU_ROW_IMPL");
+    return e ? atoi(e) : -1;
+  }();
+  const bool smem = impl == 1 || (impl != 0 && OP != kRowSum);
+  if (smem) return a.cols <= 8192 ? launch_smem<OP, 1, 256>(a, s) : launch_smem<OP, 4, 256>(a, s);
+  if (a.cols <= 8192) {
+    launch_row<OP, 512, 4>(a, s);
+    return cudaSuccess;
+  }
+  return launch_row_cluster<OP>(a, s);
+}
+
 template <int OP>
 silcu_status run_rows(const char *name, const RowArgs &a, silcu_stream stream) {
   if (a.rows == 0 || a.cols == 0) return SILCU_OK;
@@ -626,9 +822,8 @@ silcu_status run_rows(const char *name, const RowArgs &a, silcu_stream stream) {
   else if (vec && c <= 1024) launch_row_warp<OP, 8>(a, s);
   else if (vec && c <= 2048) launch_row<OP, 256, 2>(a, s);
   else if (vec && c <= 4096) launch_row<OP, 256, 4>(a, s);
-  else if (vec && c <= 8192) launch_row<OP, 512, 4>(a, s);
   else if (vec && c <= 32768 && (c % 64 == 0) && a.rows <= 0x1FFFFFFFu) {
-    const cudaError_t e = launch_row_cluster<OP>(a, s);
+    const cudaError_t e = launch_row_long<OP>(a, s);
     if (e != cudaSuccess) return fail(SILCU_CUDA_ERROR, "%s: launch: %s", name, cudaGetErrorString(e));
   } else if (vec && c <= 16384) launch_row<OP, 512, 8>(a, s);
   else if (vec && c <= 32768) launch_row<OP, 1024, 8>(a, s);

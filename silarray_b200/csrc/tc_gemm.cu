@@ -726,16 +726,20 @@ struct TcPlan {
 };
 
 // CTA pairs and tile width as above; then split K (batch 1 only) where the
-// tiles leave SMs idle:
-//  - all tiles, when they alone would fill less than 60 % of the grid (small
-//    M with N = 768, e.g. a shard of the transformer batch on 8 GPUs): up to
-//    8 parts;
-//  - otherwise only the tiles of a last, partial wave, in as many parts as
-//    keep that wave within the grid (e.g. M = 2048, N = 3072: 96 pair tiles
-//    on 74 pairs run as 74 whole tiles plus 22 tiles in 3 parts).
-// Every part keeps at least two accumulation chunks (256 k).
-// SILCU_TC_KSPLIT = 1 disables splitting, 2..8 splits every tile in that
-// many parts; SILCU_TC_TAIL = 0 disables the last-wave split (tuning).
+// tiles fill the grid's last wave poorly.  Estimated time with T tiles on U
+// persistent CTAs (pairs), a tile taking tau = 2 * 128 * BN * K FLOPs at one
+// SM's share of the 3xTF32 ceiling (276 TFLOP/s over 148 SMs):
+//   whole tiles                 ceil(T / U) tau
+//   every tile in ks parts      ceil(T ks / U) / ks tau            + finish
+//   the last wave's r tiles     (floor(T / U) + ceil(r ks / U) / ks) tau + finish
+// where finish = 3 us + (1.5 x partial bytes + the split tiles' epilogue
+// bytes) / 6.5 TB/s: the partials are written by the kernel and read back by
+// the finishing pass, which also reads the residual and writes the outputs.
+// The cheapest wins if it beats whole tiles by 5 % (the estimate's margin);
+// e.g. at M = 2048 the N = 768 GEMMs split every tile in
+// 3 parts and N = 3072 runs 74 whole pair tiles plus 22 in 3 parts.  Every
+// part keeps at least two accumulation chunks (256 k).  SILCU_TC_KSPLIT = 1
+// disables splitting, 2..8 splits every tile in that many parts (tuning).
 TcPlan tc_plan(const silcu_gemm_args &a) {
   TcPlan pl;
   const int64_t Kp = padded_k(a.K > 0 ? a.K : 1);
@@ -750,30 +754,33 @@ TcPlan tc_plan(const silcu_gemm_args &a) {
     const char *e = getenv("SILCU_TC_KSPLIT");
     return e ? atoi(e) : 0;
   }();
-  static const bool tail = [] {
-    const char *e = getenv("SILCU_TC_TAIL");
-    return !(e && atoi(e) == 0);
-  }();
-  const int64_t units = pl.pair ? sm_count() / 2 : sm_count();
-  const int64_t tiles = pl.tiles_m * pl.tiles_n * nb;
-  pl.full_items = tiles;
+  const int64_t U = pl.pair ? sm_count() / 2 : sm_count();
+  const int64_t T = pl.tiles_m * pl.tiles_n * nb;
+  pl.full_items = T;
   const int64_t nkb = (Kp + BK - 1) / BK;
-  if (nb != 1 || forced == 1) return pl;
-  auto parts = [&](int64_t ks) {
-    if (ks > 8) ks = 8;
-    while (ks > 1 && nkb / ks < 2 * CHUNK_KB_DEFAULT) ks--;  // short parts lose to the extra pass
-    return int(ks);
-  };
+  if (nb != 1 || forced == 1 || T >= (int64_t(1) << 24)) return pl;
   if (forced >= 2 && forced <= 8) {
     pl.ksplit = int(forced < nkb ? forced : nkb);
     pl.full_items = 0;
-  } else if (tiles * 10 < units * 6) {
-    pl.ksplit = parts(units / tiles);
-    pl.full_items = pl.ksplit > 1 ? 0 : tiles;
-  } else if (tail && tiles > units && tiles % units != 0) {
-    const int64_t rem = tiles % units;
-    pl.ksplit = parts(units / rem);
-    pl.full_items = pl.ksplit > 1 ? tiles - rem : tiles;
+    return pl;
+  }
+  const double tau = 2.0 * BM * pl.BN * double(Kp) / (276e12 / 148) * 1e6;  // us
+  const double tile_elems = double(pl.TM) * pl.BN;
+  const double epi_bytes = tile_elems * ((a.C ? 4 : 0) + (a.C_hi && a.C_lo ? 8 : 0) + (a.residual ? 4 : 0));
+  auto cdiv = [](int64_t x, int64_t y) { return (x + y - 1) / y; };
+  auto finish = [&](int64_t tiles, int ks) {
+    return 3.0 + (1.5 * 4.0 * tile_elems * double(tiles) * ks + epi_bytes * double(tiles)) / 6.5e12 * 1e6;
+  };
+  const double whole = double(cdiv(T, U)) * tau;
+  double best = 0.95 * whole;
+  const int64_t r = T % U;
+  for (int ks = 2; ks <= 8 && nkb / ks >= 2 * CHUNK_KB_DEFAULT; ks++) {
+    const double all = double(cdiv(T * ks, U)) / ks * tau + finish(T, ks);
+    if (all < best) best = all, pl.ksplit = ks, pl.full_items = 0;
+    if (r != 0 && T > U) {
+      const double tail = (double(T / U) + double(cdiv(r * ks, U)) / ks) * tau + finish(r, ks);
+      if (tail < best) best = tail, pl.ksplit = ks, pl.full_items = T - r;
+    }
   }
   return pl;
 }

@@ -59,8 +59,12 @@ def test_sum_i32_wraps(cuda):
 
 @pytest.mark.parametrize("rows,cols", [(1, 1), (5, 3), (64, 300), (33, 128), (4, 1000), (17, 1024),
                                        (8, 2048), (8, 4096), (8, 8192), (4, 16384), (3, 32768),
-                                       (2, 40000), (2, 40001)])
+                                       (2, 40000), (2, 40001), (1000, 8192), (700, 16384), (600, 32768),
+                                       (301, 8256)])
 def test_row_ops(cuda, rows, cols):
+    """Row ops against the oracle.  Rows of 4K-32K columns (multiples of 64)
+    run on a persistent grid where each CTA / cluster prefetches its next
+    row; the many-row cases give every CTA several rows."""
     rng = np.random.default_rng(rows * 100003 + cols)
     x = rng.normal(0, 2, (rows, cols)).astype(np.float32)
     X = dev(x)
