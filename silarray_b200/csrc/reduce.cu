@@ -401,8 +401,8 @@ __global__ void __launch_bounds__(NT) row_smem_kernel(const RowArgs a) {
   namespace cg = cooperative_groups;
   __shared__ float sf[NT / 32];
   __shared__ unsigned long long sk[NT / 32];
-  __shared__ float xf[2];
-  __shared__ unsigned long long xk;
+  __shared__ float xf[2][CL];                 // slot, source rank
+  __shared__ unsigned long long xk[CL];
   const int t = threadIdx.x;
   uint32_t rank = 0;
   if constexpr (CL > 1) rank = cg::this_cluster().block_rank();
@@ -420,21 +420,29 @@ __global__ void __launch_bounds__(NT) row_smem_kernel(const RowArgs a) {
                  "l"(src), "r"(part * 16), "r"(bar)
                  : "memory");
   }
+  // Cluster peers must have started before anyone writes into their shared
+  // memory: arrive now, wait just before the first exchange.
+  if constexpr (CL > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   __syncthreads();
   // A failed wait (error word set) computes on whatever is in shared memory;
   // the host reads the status.  Every thread waits, so none reads early.
   tc::mbar_wait(bar, 0, a.err, 41);
+  bool started = false;
+  // Cluster exchange, push form: every CTA writes its partial into slot
+  // [slot][rank] of every CTA of the cluster, one cluster barrier, then each
+  // combines its local copies in rank order (the same result everywhere).
+  // No CTA reads another's shared memory, so none has to wait for its peers
+  // before leaving; each slot is written once per CTA.
   auto cl_combine = [&](float x, int slot, bool is_max) {
     if constexpr (CL > 1) {
       cg::cluster_group cl = cg::this_cluster();
-      if (t == 0) xf[slot] = x;
+      if (!started) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+      started = true;
+      if (t < CL) *cl.map_shared_rank(&xf[slot][rank], uint32_t(t)) = x;
       cl.sync();
       float r = is_max ? __int_as_float(0xff800000) : 0.f;
 #pragma unroll
-      for (int q = 0; q < CL; q++) {
-        const float y = *cl.map_shared_rank(&xf[slot], q);
-        r = is_max ? fmaxf(r, y) : r + y;
-      }
+      for (int q = 0; q < CL; q++) r = is_max ? fmaxf(r, xf[slot][q]) : r + xf[slot][q];
       return r;
     }
     return x;
@@ -513,21 +521,18 @@ __global__ void __launch_bounds__(NT) row_smem_kernel(const RowArgs a) {
     }
     unsigned long long best = bi >= 0 ? amax_key(bv, uint32_t(bi)) : 0ull;
     best = block_reduce<NT>(best, sk, Max());
-    if constexpr (CL > 1) {
+    if constexpr (CL > 1) {  // push to rank 0 only: it alone writes the index
       cg::cluster_group cl = cg::this_cluster();
-      if (t == 0) xk = best;
+      asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+      if (t == 0) *cl.map_shared_rank(&xk[rank], 0u) = best;
       cl.sync();
       if (rank == 0 && t == 0) {
 #pragma unroll
-        for (int q = 0; q < CL; q++) {
-          const unsigned long long k = *cl.map_shared_rank(&xk, q);
-          best = best > k ? best : k;
-        }
+        for (int q = 0; q < CL; q++) best = best > xk[q] ? best : xk[q];
       }
     }
     if (rank == 0 && t == 0) a.idx[row] = best ? int32_t(0xFFFFFFFFu - uint32_t(best & 0xFFFFFFFFu)) : 0;
   }
-  if constexpr (CL > 1) cg::this_cluster().sync();  // peers may still be reading this CTA's exchange slots
 }
 
 // Long rows: a cluster of CL CTAs shares one row (each holds 1/CL of it in
@@ -788,19 +793,29 @@ cudaError_t launch_smem(RowArgs a, cudaStream_t s) {
 }
 
 // Rows of 4K-32K columns (multiples of 64): softmax, layer_norm and argmax
-// from shared memory (measured at 4096 x 8192: 0.95 / 0.88 / 0.92 of HBM
-// against 0.93 / 0.79 / 0.89 with the row in registers; at 4096 x 32768
-// 0.70 / 0.69 / 0.76 against 0.69 / 0.64 / 0.76); the row sum from
-// registers (0.97 / 0.98 against 0.94 / 0.77).  SILCU_ROW_IMPL = 0 / 1
-// forces registers / shared memory (tuning).
+// from shared memory, one CTA per row up to 8K columns and a 2-CTA cluster
+// above (measured at 4096 x 8192: 0.95 / 0.87 / 0.90 of HBM against
+// 0.93 / 0.79 / 0.89 with the row in registers; at 4096 x 32768
+// 0.77 / 0.74 / 0.82 against 0.69 / 0.64 / 0.76; clusters of 4: 0.76 /
+// 0.74 / 0.80); the row sum from registers (0.97 / 0.98 against 0.94 /
+// 0.77).  SILCU_ROW_IMPL = 0 / 1 forces registers / shared memory,
+// SILCU_ROW_SMEM_CL = 4 the larger cluster (tuning).
 template <int OP>
 cudaError_t launch_row_long(const RowArgs &a, cudaStream_t s) {
   static const int impl = [] {
     const char *e = getenv("SILCU_ROW_IMPL");
     return e ? atoi(e) : -1;
   }();
+  static const int cl = [] {  // cluster size of the shared-memory kernel above 8K columns
+    const char *e = getenv("SILCU_ROW_SMEM_CL");
+    const int v = e ? atoi(e) : 2;
+    return v == 4 ? 4 : 2;
+  }();
   const bool smem = impl == 1 || (impl != 0 && OP != kRowSum);
-  if (smem) return a.cols <= 8192 ? launch_smem<OP, 1, 256>(a, s) : launch_smem<OP, 4, 256>(a, s);
+  if (smem) {
+    if (a.cols <= 8192) return launch_smem<OP, 1, 256>(a, s);
+    return cl == 4 ? launch_smem<OP, 4, 256>(a, s) : launch_smem<OP, 2, 512>(a, s);
+  }
   if (a.cols <= 8192) {
     launch_row<OP, 512, 4>(a, s);
     return cudaSuccess;

@@ -19,6 +19,7 @@ sequence x head through strided views), Wo gemm (+bias +residual),
 layer_norm, W1 gemm (+bias, relu), W2 gemm (+bias +residual).  Every
 product is 3xTF32 on tcgen05.
 """
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -95,9 +96,15 @@ class Block:
     attention reads Q, K and V in place from the QKV output (V as the MN-major
     operand of its P.V product)."""
 
-    def __init__(self, cfg, params, device="cuda"):
+    def __init__(self, cfg, params, device="cuda", graphs=None):
         self.cfg = cfg
         self.dev = torch.device(device)
+        # Each distinct (input, output, sequence range) runs eagerly once, is
+        # then captured as a CUDA graph of its launches and replayed from then
+        # on (SILCU_GRAPHS=0 or graphs=False: always eager).
+        self.graphs = (os.environ.get("SILCU_GRAPHS", "1") != "0") if graphs is None else bool(graphs)
+        self._graph_cache = {}
+        self.replayed_launches = 0  # kernels launched by graph replays (the library counts the rest)
         t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(self.dev)  # noqa: E731
         d, f = cfg.d_model, cfg.d_ff
         self.g1, self.be1, self.g2, self.be2 = t(params["g1"]), t(params["be1"]), t(params["g2"]), t(params["be2"])
@@ -126,7 +133,7 @@ class Block:
         cfg = self.cfg
         x = x.reshape(-1)
         out = torch.empty(cfg.tokens * cfg.d_model, dtype=torch.float32, device=self.dev) if out is None else out
-        self._forward_seqs(x, out.reshape(-1), 0, cfg.batch)
+        self._run(x, out.reshape(-1), 0, cfg.batch)
         return out.reshape(cfg.tokens, cfg.d_model)
 
     def forward_host(self, x_host, out_host, chunks=2):
@@ -166,7 +173,7 @@ class Block:
         for c in range(chunks):
             r0, r1 = bounds[c] * S * d, bounds[c + 1] * S * d
             comp.wait_event(ready[c])
-            self._forward_seqs(self._x_dev, self._o_dev, bounds[c], bounds[c + 1] - bounds[c])
+            self._run(self._x_dev, self._o_dev, bounds[c], bounds[c + 1] - bounds[c])
             done = torch.cuda.Event()
             done.record(comp)
             self._s_out.wait_event(done)
@@ -214,7 +221,7 @@ class Block:
             comp.wait_event(ready)
             if copied_out[i] is not None:
                 comp.wait_event(copied_out[i])  # dout[i] read out for batch k - 2
-            self._forward_seqs(din[i], dout[i], 0, cfg.batch)
+            self._run(din[i], dout[i], 0, cfg.batch)
             done = torch.cuda.Event()
             done.record(comp)
             computed[i] = done
@@ -227,6 +234,34 @@ class Block:
         comp.wait_stream(self._s_out2)
         comp.wait_stream(self._s_in2)
         return out_hosts
+
+    def _run(self, x, out, b0, nb):
+        """_forward_seqs on the current stream, through a CUDA graph per
+        (x, out, b0, nb) once that combination has run eagerly: the replay
+        launches the same kernels with the same arguments, without the
+        per-launch host work.  The graph keeps the shared workspace it was
+        captured with alive (a later, larger request replaces the cached
+        buffer but not this one)."""
+        need = (b0 + nb) * self.cfg.seq * self.cfg.d_model
+        on_dev = lambda t: t.device.type == self.dev.type and self.dev.index in (None, t.device.index)  # noqa: E731
+        if x.numel() < need or out.numel() < need or not on_dev(x) or not on_dev(out):
+            raise ValueError("Block: input / output must be device tensors of cfg.tokens x d_model floats")
+        if not self.graphs:
+            self._forward_seqs(x, out, b0, nb)
+            return
+        key = (x.data_ptr(), out.data_ptr(), b0, nb)
+        g = self._graph_cache.get(key)
+        if g is None:
+            self._forward_seqs(x, out, b0, nb)  # sizes the workspace, sets kernel attributes, computes out
+            graph = torch.cuda.CUDAGraph()
+            n0 = gpu.lib().silcu_kernel_launches()
+            with torch.cuda.graph(graph):
+                self._forward_seqs(x, out, b0, nb)
+            n = gpu.lib().silcu_kernel_launches() - n0
+            self._graph_cache[key] = (graph, n, gpu.workspace(0, self.dev))
+            return
+        g[0].replay()
+        self.replayed_launches += g[1]
 
     def _forward_seqs(self, x, out, b0, nb):
         """Sequences [b0, b0 + nb) of the batch: every operand and activation

@@ -70,3 +70,25 @@ def test_forward_host_stream(cuda):
     for k in range(5):
         np.testing.assert_array_equal(got[k].reshape(want[k].shape), want[k])
     gpu.device_status()
+
+
+def test_graph_replay_matches_eager(cuda):
+    """The second and later forwards over the same buffers replay a CUDA graph
+    of the first one's launches: bit for bit the eager result, also after the
+    input changes in place, and the replayed kernels are counted."""
+    cfg = transformer.Config(batch=2, seq=256, d_model=256, heads=4, d_ff=1024)
+    p = transformer.init_params(cfg, seed=8)
+    eager = transformer.Block(cfg, p, device="cuda", graphs=False)
+    graphed = transformer.Block(cfg, p, device="cuda", graphs=True)
+    x = torch.from_numpy(transformer.init_input(cfg, seed=9)).cuda()
+    out = torch.empty(cfg.tokens * cfg.d_model, device="cuda")
+    for step in range(3):
+        if step == 2:
+            x.mul_(0.5)  # new content, same buffer: the replay reads it
+        want = eager.forward(x).cpu().numpy()
+        got = graphed.forward(x, out).cpu().numpy()
+        np.testing.assert_array_equal(got, want)
+    assert graphed.replayed_launches > 0
+    with pytest.raises(ValueError):
+        graphed.forward(x.reshape(-1)[: x.numel() // 2], out)
+    gpu.device_status()
