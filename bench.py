@@ -13,7 +13,9 @@ N > 1 is launched by torchrun (one process per GPU, NCCL for the barrier and
 the max-over-ranks time; the forward itself needs no collective).
 Timing: CUDA events on the launching stream around each step; the 126 MB L2
 is flushed (256 MiB write) before every timed step; W >= 3 untimed warm-ups;
-nvidia-smi clocks are sampled during the timed region.
+nvidia-smi clocks are sampled during the timed region.  Block.forward runs
+eagerly once per buffer set (warm-up) and then replays a CUDA graph of the
+same launches; gpu_launches counts the kernels those replays launch.
 """
 import argparse
 import json
@@ -506,7 +508,8 @@ def run_ours(args):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "transformer_block_fwd", "global_batch": full.batch, "seq_len": full.seq,
                        "d_model": full.d_model, "heads": full.heads, "d_ff": full.d_ff,
-                       "parallelism": f"dp{world}", "l2": "flushed (256 MiB write) before every timed step"},
+                       "parallelism": f"dp{world}", "l2": "flushed (256 MiB write) before every timed step",
+                       "launch": "CUDA-graph replay of the forward's kernels (captured after its first eager run)"},
             "clocks": clocks, "e2e": e2e, "gpu_launches": int(launches), "roofline": roofline,
             "sgemm_8192": sg, "cpu_baseline": cpu,
         }

@@ -13,11 +13,13 @@ rounding sequence per element is the reference's (dot, then + bias, then
 act, then + residual).  Q, K and V come from one GEMM against [Wq|Wk|Wv]
 (columns are independent, so the values equal three separate GEMMs).
 
-Launches per forward: layer_norm, QKV gemm, V^T split, fused attention
-(scores, softmax and the context product in one tcgen05 kernel, per
-sequence x head through strided views), Wo gemm (+bias +residual),
-layer_norm, W1 gemm (+bias, relu), W2 gemm (+bias +residual).  Every
-product is 3xTF32 on tcgen05.
+Launches per forward: layer_norm, QKV gemm, fused attention (scores,
+softmax and the context product in one tcgen05 kernel, per sequence x head,
+Q, K and V read in place through strided views), Wo gemm (+bias +residual),
+layer_norm, W1 gemm (+bias, relu), W2 gemm (+bias +residual); a GEMM whose
+tiles fill its last wave poorly adds one finishing pass for its split-K
+tiles.  Every product is 3xTF32 on tcgen05.  After the first forward over a
+given set of buffers, the launches replay as one CUDA graph.
 """
 import os
 from dataclasses import dataclass
@@ -265,8 +267,8 @@ class Block:
 
     def _forward_seqs(self, x, out, b0, nb):
         """Sequences [b0, b0 + nb) of the batch: every operand and activation
-        is the view of those rows (heads of those sequences for V^T), so the
-        groups of a chunked forward share nothing."""
+        is the view of those rows, so the groups of a chunked forward share
+        nothing."""
         cfg = self.cfg
         d, f, S, H, hd = cfg.d_model, cfg.d_ff, cfg.seq, cfg.heads, cfg.head_dim
         T = nb * S
