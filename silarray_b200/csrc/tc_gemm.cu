@@ -168,7 +168,10 @@ __device__ __forceinline__ void stage_row_swz(float *st, int lane, const float (
 // shared memory and write each CTA's TMEM, waits on its own ring barriers
 // (which also count the peer's TMA bytes) and commits to the barriers of both
 // CTAs; both CTAs' epilogue warps release the accumulator buffers to it.
-template <int BN_, bool PAIR>
+// SPLIT: the launch has split-K tiles (full_items < all tiles).  Launches
+// without them use the SPLIT = false instance, which has none of the part
+// logic and so the register allocation of the plain epilogue.
+template <int BN_, bool PAIR, bool SPLIT>
 __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
   using C = Cfg<BN_, PAIR>;
   constexpr int BN = C::BN, STAGES = C::STAGES, NBUF = C::NBUF, RING_BYTES = C::RING_BYTES;
@@ -192,8 +195,10 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
   const int nk = (p.K + BK - 1) / BK;
   const int CHUNK_KB = p.chunk_kb;
   // K blocks [kb0, kb1) of a work item, and its number of accumulation chunks.
-  auto item_tile = [&](int item) { return item < p.full_items ? item : p.full_items + (item - p.full_items) / p.ksplit; };
-  auto item_part = [&](int item) { return item < p.full_items ? -1 : (item - p.full_items) % p.ksplit; };
+  auto item_tile = [&](int item) {
+    return (!SPLIT || item < p.full_items) ? item : p.full_items + (item - p.full_items) / p.ksplit;
+  };
+  auto item_part = [&](int item) { return (!SPLIT || item < p.full_items) ? -1 : (item - p.full_items) % p.ksplit; };
   auto k_range = [&](int item, int &kb0, int &kb1) {
     const int ks = item_part(item);
     kb0 = ks < 0 ? 0 : ks * nk / p.ksplit;
@@ -367,7 +372,7 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
       const bool good = __all_sync(0xffffffffu, ok && *reinterpret_cast<volatile int *>(p.err) == 0);
       if (!good) break;
       const int part = item_part(tile);
-      if (part >= 0) {
+      if (SPLIT && part >= 0) {
         // A K part of a split tile: its plain partial, no epilogue.
         if (m0 + 32 * q >= p.M) continue;
 #pragma unroll
@@ -653,14 +658,14 @@ __global__ void __launch_bounds__(256) split_contig(const float *__restrict__ sr
 // ---------------------------------------------------------------- host side
 int64_t padded_k(int64_t K) { return ((K + KPAD - 1) / KPAD) * KPAD; }
 
-template <int BN, bool PAIR>
+template <int BN, bool PAIR, bool SPLIT>
 silcu_status launch_tc(const TcParams &p, uint32_t grid, cudaStream_t s) {
   using C = Cfg<BN, PAIR>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, PAIR, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::SMEM_BYTES);
     if (e != cudaSuccess) return fail(SILCU_CUDA_ERROR, "sgemm(tc): smem attribute: %s", cudaGetErrorString(e));
     configured[dev] = true;
@@ -677,7 +682,7 @@ silcu_status launch_tc(const TcParams &p, uint32_t grid, cudaStream_t s) {
   at[0].val.clusterDim.z = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, PAIR>, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, PAIR, SPLIT>, p);
   if (e != cudaSuccess) return fail(SILCU_CUDA_ERROR, "sgemm(tc): launch: %s", cudaGetErrorString(e));
   return check_launch("sgemm(tc)");
 }
@@ -1013,17 +1018,18 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
   }
   const int64_t total = plan.full_items + split_tiles * plan.ksplit;
   silcu_status st;
+  const bool split = plan.ksplit > 1;
   if (pair) {
     const int64_t pairs = sm_count() / 2;
     const uint32_t grid = uint32_t(2 * (total < pairs ? total : pairs));
-    if (BN == 256) st = launch_tc<256, true>(p, grid, s);
-    else if (BN == 128) st = launch_tc<128, true>(p, grid, s);
-    else st = launch_tc<64, true>(p, grid, s);
+    if (BN == 256) st = split ? launch_tc<256, true, true>(p, grid, s) : launch_tc<256, true, false>(p, grid, s);
+    else if (BN == 128) st = split ? launch_tc<128, true, true>(p, grid, s) : launch_tc<128, true, false>(p, grid, s);
+    else st = split ? launch_tc<64, true, true>(p, grid, s) : launch_tc<64, true, false>(p, grid, s);
   } else {
     const uint32_t grid = uint32_t(total < sm_count() ? total : sm_count());
-    if (BN == 256) st = launch_tc<256, false>(p, grid, s);
-    else if (BN == 128) st = launch_tc<128, false>(p, grid, s);
-    else st = launch_tc<64, false>(p, grid, s);
+    if (BN == 256) st = split ? launch_tc<256, false, true>(p, grid, s) : launch_tc<256, false, false>(p, grid, s);
+    else if (BN == 128) st = split ? launch_tc<128, false, true>(p, grid, s) : launch_tc<128, false, false>(p, grid, s);
+    else st = split ? launch_tc<64, false, true>(p, grid, s) : launch_tc<64, false, false>(p, grid, s);
   }
   if (st != SILCU_OK || plan.ksplit == 1) return st;
   TcEpi epi;
