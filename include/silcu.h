@@ -264,8 +264,9 @@ silcu_status silcu_attention_f32(const silcu_attention_args *args_host, silcu_st
 /* The general GEMM of the reference's dot / linear / linear_sigmoid /
  * batched_dot nodes.  The workspace (size from silcu_sgemm_workspace_bytes,
  * 0 when none is needed) holds the tf32 splits of operands given plain and,
- * when a few long-K output tiles are cut into K parts, their partial sums;
- * results are deterministic (fixed summation order). */
+ * when output tiles that would leave SMs idle (few tiles, or a partial last
+ * wave) are cut into K parts, those tiles' partial sums; results are
+ * deterministic (fixed summation order for a given shape and GPU). */
 size_t silcu_sgemm_workspace_bytes(const silcu_gemm_args *args_host);
 silcu_status silcu_sgemm_ex(const silcu_gemm_args *args_host, void *workspace, size_t workspace_bytes,
                             silcu_stream stream);
