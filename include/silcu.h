@@ -268,6 +268,16 @@ silcu_status silcu_attention_f32(const silcu_attention_args *args_host, silcu_st
  * wave) are cut into K parts, those tiles' partial sums; results are
  * deterministic (fixed summation order for a given shape and GPU). */
 size_t silcu_sgemm_workspace_bytes(const silcu_gemm_args *args_host);
+/* How silcu_sgemm_ex runs these arguments (diagnostics and tests: no GPU
+ * work, no allocation, no pointer is dereferenced).  path: 0 = CUDA-core FFMA
+ * tiles, 1 = GEMV / small-M kernels, 2 = 3xTF32 tensor cores; for path 2 the
+ * output-tile width, CTA pairs (256-row tiles), the number of output tiles,
+ * how many of them run whole and in how many K parts the others run. */
+typedef struct {
+  int32_t path, pair, tile_n, ksplit;
+  int64_t tiles, whole_tiles;
+} silcu_gemm_plan;
+silcu_status silcu_sgemm_plan(const silcu_gemm_args *args_host, silcu_gemm_plan *plan);
 silcu_status silcu_sgemm_ex(const silcu_gemm_args *args_host, void *workspace, size_t workspace_bytes,
                             silcu_stream stream);
 /* Thin forms with the reference's argument lists. */

@@ -53,6 +53,10 @@ class GemmArgs(C.Structure):
                 ("A_hi", vp), ("A_lo", vp), ("B_hi", vp), ("B_lo", vp), ("C_hi", vp), ("C_lo", vp)]
 
 
+class GemmPlan(C.Structure):
+    _fields_ = [("path", i32), ("pair", i32), ("tile_n", i32), ("ksplit", i32), ("tiles", i64), ("whole_tiles", i64)]
+
+
 class AttnArgs(C.Structure):
     _fields_ = [("Q_hi", vp), ("Q_lo", vp), ("K_hi", vp), ("K_lo", vp), ("Vt_hi", vp), ("Vt_lo", vp),
                 ("O", vp), ("O_hi", vp), ("O_lo", vp),
@@ -95,6 +99,7 @@ _SIGS = {
     "silcu_sum_axis_workspace_bytes": ([sz, sz, sz], sz),
     "silcu_sum_axis_f32": ([vp, vp, sz, sz, sz, vp, sz, vp], C.c_int),
     "silcu_sgemm_workspace_bytes": ([C.POINTER(GemmArgs)], sz),
+    "silcu_sgemm_plan": ([C.POINTER(GemmArgs), C.POINTER(GemmPlan)], C.c_int),
     "silcu_sgemm_ex": ([C.POINTER(GemmArgs), vp, sz, vp], C.c_int),
     "silcu_sgemm": ([vp, vp, vp, u32, u32, u32, u32, u32, C.c_int, C.c_int, vp, sz, vp], C.c_int),
     "silcu_sgemm_batched": ([vp, vp, vp, u32, u32, u32, u32, u32, u32, u64, u64, u64, vp, sz, vp], C.c_int),

@@ -619,6 +619,16 @@ size_t silcu_sgemm_workspace_bytes(const silcu_gemm_args *a) {
   }
 }
 
+silcu_status silcu_sgemm_plan(const silcu_gemm_args *a, silcu_gemm_plan *plan) {
+  if (!a || !plan) return fail(SILCU_INVALID_ARGUMENT, "sgemm_plan: null argument");
+  silcu_gemm_plan p = {};
+  p.path = gemm_path(*a);
+  p.ksplit = 1;
+  if (p.path == kPathTc) tc_describe(*a, &p);
+  *plan = p;
+  return SILCU_OK;
+}
+
 silcu_status silcu_sgemm_ex(const silcu_gemm_args *ap, void *ws, size_t wsb, silcu_stream stream) {
   if (!ap) return fail(SILCU_INVALID_ARGUMENT, "sgemm: null args");
   const silcu_gemm_args &a = *ap;

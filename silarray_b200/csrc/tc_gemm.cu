@@ -877,6 +877,15 @@ __global__ void __launch_bounds__(256) tile_finish(const float *__restrict__ par
 
 }  // namespace
 
+void tc_describe(const silcu_gemm_args &a, silcu_gemm_plan *out) {
+  const TcPlan pl = tc_plan(a);
+  out->pair = pl.pair ? 1 : 0;
+  out->tile_n = pl.BN;
+  out->ksplit = pl.ksplit;
+  out->tiles = pl.tiles_m * pl.tiles_n * total_batch(a);
+  out->whole_tiles = pl.full_items;
+}
+
 size_t tc_workspace_bytes(const silcu_gemm_args &a) {
   const int64_t Kp = padded_k(a.K > 0 ? a.K : 1);
   size_t bytes = 256;

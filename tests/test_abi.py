@@ -73,3 +73,50 @@ def test_python_mirror_refuses_cpu_tensors():
     from silarray_b200 import gpu
     with pytest.raises(TypeError):
         gpu.add(torch.ones(4), torch.ones(4))
+
+
+def _plan(lib, M, N, K, split_in=True, c=True, split_out=False, residual=False, trans_b=1):
+    a = _lib.GemmArgs()
+    a.M, a.N, a.K = M, N, K
+    a.lda, a.ldb, a.ldc, a.ldr = K, (K if trans_b else N), N, N
+    a.trans_b = trans_b
+    a.batch, a.batch_inner = 1, 1
+    a.alpha = 1.0
+    fake = C.c_void_p(1 << 20)  # never dereferenced by the planner
+    if split_in:
+        a.A_hi = a.A_lo = a.B_hi = a.B_lo = fake
+    else:
+        a.A = a.B = fake
+    if c:
+        a.C = fake
+    if split_out:
+        a.C_hi = a.C_lo = fake
+    if residual:
+        a.residual = fake
+    p = _lib.GemmPlan()
+    assert lib.silcu_sgemm_plan(C.byref(a), C.byref(p)) == 0
+    return p
+
+
+def test_gemm_plan_split_k_choice(lib):
+    """The 3xTF32 path's split-K choice on a 148-SM B200 (the library assumes
+    148 SMs when it cannot query a device) for the transformer's GEMMs: at a
+    4-sequence shard (M = 2048) the N = 768 GEMMs split every tile in 3 K
+    parts and FFN-up splits only its last wave's 22 pair tiles; at the full
+    batch (M = 16384) FFN-down splits its last wave's 44 tiles in 5 parts,
+    the other GEMMs none."""
+    p = _plan(lib, 2048, 768, 768, residual=True)  # Wo
+    assert (p.path, p.pair, p.tile_n, p.ksplit, p.tiles, p.whole_tiles) == (2, 0, 256, 3, 48, 0)
+    p = _plan(lib, 2048, 3072, 768, c=False, split_out=True)  # FFN-up, split output
+    assert (p.pair, p.ksplit, p.tiles, p.whole_tiles) == (1, 3, 96, 74)
+    p = _plan(lib, 2048, 768, 3072, residual=True)  # FFN-down
+    assert (p.pair, p.ksplit, p.whole_tiles) == (0, 3, 0)
+    p = _plan(lib, 16384, 768, 3072, residual=True)  # FFN-down, full batch
+    assert (p.pair, p.ksplit, p.tiles, p.whole_tiles) == (1, 5, 192, 148)
+    for M, N, K in [(16384, 2304, 768), (16384, 3072, 768), (16384, 768, 768)]:
+        p = _plan(lib, M, N, K, c=False, split_out=True)
+        assert (p.pair, p.ksplit, p.whole_tiles) == (1, 1, p.tiles), (M, N, K)
+    p = _plan(lib, 8192, 8192, 8192, split_in=False)  # the 8192^3 SGEMM: plain operands, no split
+    assert (p.path, p.pair, p.ksplit) == (2, 1, 1)
+    p = _plan(lib, 1, 4096, 4096, split_in=False, trans_b=0)  # GEMV: x . W[K, N]
+    assert p.path == 1
