@@ -763,7 +763,7 @@ TcPlan tc_plan(const silcu_gemm_args &a) {
   const int64_t T = pl.tiles_m * pl.tiles_n * nb;
   pl.full_items = T;
   const int64_t nkb = (Kp + BK - 1) / BK;
-  if (nb != 1 || forced == 1 || T >= (int64_t(1) << 24)) return pl;
+  if (nb != 1 || forced == 1 || T > 65535) return pl;  // the finishing pass's grid.y counts split tiles
   if (forced >= 2 && forced <= 8) {
     pl.ksplit = int(forced < nkb ? forced : nkb);
     pl.full_items = 0;
