@@ -42,7 +42,7 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--suite", action="store_true",
                     help="measure every configuration of the metric (one JSON line each) instead of the headline")
-    ap.add_argument("--profile-case", default=None, choices=["gemm", "block", "attention"],
+    ap.add_argument("--profile-case", default=None, choices=["gemm", "block", "attention", "hbm"],
                     help="run only a small case for ncu: the FFN-up GEMM of the workload, or a 2-sequence block")
     return ap.parse_args()
 
@@ -64,7 +64,11 @@ def ffn_up_case(dev, T=16384, d=768, f=3072):
 def profile_case(args):
     """Small, self-terminating cases for ncu captures (one GPU): `gemm` runs the
     dominant kernel as the forward does (FFN-up, M=16384 N=3072 K=768, ~600 MB
-    on the device) warmup+1 times; `block` runs a 2-sequence transformer forward."""
+    on the device) warmup+1 times; `block` runs a 2-sequence transformer forward;
+    `attention` the fused attention on a quarter of the BMM-attention config;
+    `hbm` the HBM-bound kernels of the suite once each after the warm-ups
+    (GEMV 1x4096.4096x4096, softmax / layer_norm 4096x8192 and 4096x32768,
+    argmax 4096x32768, global sum 2^28: ~2.5 GB on the device)."""
     import torch
     from silarray_b200 import gpu, transformer
     dev = torch.device("cuda", 0)
@@ -82,6 +86,23 @@ def profile_case(args):
         for _ in range(args.warmup + 1):
             gpu.attention(qs, ks, vt, Sq=S, Sk=S, batch=BH, heads=1, ldq=d, sq_b=S * d, sq_h=S * d, ldk=d,
                           sk_b=S * d, sk_h=S * d, ldv=S, sv_b=d * S, sv_h=d * S, scale=0.125, O=Ob)
+    elif args.profile_case == "hbm":
+        g = torch.Generator(device=dev).manual_seed(0)
+        x, W, bb, y = (torch.randn(4096, device=dev, generator=g), torch.randn(4096 * 4096, device=dev, generator=g),
+                       torch.randn(4096, device=dev, generator=g), torch.empty(4096, device=dev))
+        r8 = torch.randn(4096 * 8192, device=dev, generator=g) * 2
+        r32 = torch.randn(4096 * 32768, device=dev, generator=g) * 2
+        o32 = torch.empty_like(r32)
+        gm, bt = torch.ones(32768, device=dev), torch.zeros(32768, device=dev)
+        flat = torch.rand(1 << 28, device=dev, generator=g) * 2 - 1
+        for _ in range(args.warmup + 1):
+            gpu.sgemv(x, W, y, 4096, 4096, bias=bb)
+            gpu.softmax(r8, o32[: r8.numel()], rows=4096, cols=8192)
+            gpu.layer_norm(r8, o32[: r8.numel()], gamma=gm[:8192], beta=bt[:8192], rows=4096, cols=8192)
+            gpu.softmax(r32, o32, rows=4096, cols=32768)
+            gpu.layer_norm(r32, o32, gamma=gm, beta=bt, rows=4096, cols=32768)
+            gpu.argmax_f32(r32, rows=4096, cols=32768)
+            gpu.sum_f32(flat)
     else:
         cfg = transformer.Config(batch=2)
         blk = transformer.Block(cfg, transformer.init_params(cfg), device=dev)
