@@ -219,3 +219,20 @@ def test_tc_split_k(cuda, M, N, K):
                           algo="tc")).reshape(M, N)
     np.testing.assert_array_equal(again, got)
     gpu.device_status()
+
+
+def test_tc_split_last_wave_full_batch(cuda):
+    """The full-batch FFN-down shape (M = 16384, N = 768, K = 3072, bias +
+    residual): 148 whole pair tiles, then the last wave's 44 tiles in 5 K parts
+    (rows 12288 and up hold most of them), summed by the finishing pass."""
+    M, N, K = 16384, 768, 3072
+    rng = np.random.default_rng(11)
+    a = rng.standard_normal((M, K), dtype=np.float32)
+    b = (rng.standard_normal((K, N), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    bias = rng.uniform(-1, 1, N).astype(np.float32)
+    res = rng.uniform(-1, 1, (M, N)).astype(np.float32)
+    got = host(gpu.gemm(dev(a), dev(b), M=M, N=N, K=K, bias=dev(bias), residual=dev(res), algo="tc")).reshape(M, N)
+    rows = [0, 255, 4096, 12287, 12288, 12300, 13000, 14000, 15000, 16000, 16383]
+    ref = a[rows].astype(np.float64) @ b.astype(np.float64) + bias + res[rows]
+    assert_dot_close(got[rows], ref, K, what="split last wave 16384x768x3072")
+    gpu.device_status()
