@@ -98,6 +98,8 @@ class Block:
     attention reads Q, K and V in place from the QKV output (V as the MN-major
     operand of its P.V product)."""
 
+    MAX_GRAPHS = 8  # captured buffer sets kept (the oldest is dropped beyond this)
+
     def __init__(self, cfg, params, device="cuda", graphs=None):
         self.cfg = cfg
         self.dev = torch.device(device)
@@ -260,6 +262,8 @@ class Block:
             with torch.cuda.graph(graph):
                 self._forward_seqs(x, out, b0, nb)
             n = gpu.lib().silcu_kernel_launches() - n0
+            if len(self._graph_cache) >= self.MAX_GRAPHS:  # bounded: drop the oldest capture
+                self._graph_cache.pop(next(iter(self._graph_cache)))
             self._graph_cache[key] = (graph, n, gpu.workspace(0, self.dev))
             return
         g[0].replay()
