@@ -330,6 +330,22 @@ def peaks():
 
 
 # ------------------------------------------------------------ CPU baseline
+def workload_config(full, world):
+    """The `config` both arms report (identical keys and values at a given N)."""
+    return {"workload": "transformer_block_fwd", "global_batch": full.batch, "seq_len": full.seq,
+            "d_model": full.d_model, "heads": full.heads, "d_ff": full.d_ff, "parallelism": f"dp{world}",
+            "l2": "GPU arm: flushed (256 MiB write) before every timed step"}
+
+
+def _reference_sequence(one, params, x, k):
+    """One bounded sample of the workload on the reference CPU path: sequence
+    k % batch of the batch (512 tokens through the whole block)."""
+    from oracle import transformer_ref as TR
+    n = x.shape[0] // one.seq
+    i = k % n
+    TR.reference_forward(one, params, x[i * one.seq:(i + 1) * one.seq])
+
+
 def cpu_baseline(cfg, params, x, budget_s=12.0):
     """The reference's own CPU implementation of the block (oracle/_ref, all
     host threads for cblas_sgemm) on a bounded sample: whole sequences of the
@@ -340,8 +356,7 @@ def cpu_baseline(cfg, params, x, budget_s=12.0):
     one = transformer.Config(batch=1, seq=cfg.seq, d_model=cfg.d_model, heads=cfg.heads, d_ff=cfg.d_ff)
     n, t0 = 0, time.perf_counter()
     while True:
-        xs = x[n * cfg.seq:(n + 1) * cfg.seq]
-        transformer.reference_forward(one, params, xs)
+        _reference_sequence(one, params, x, n)
         n += 1
         el = time.perf_counter() - t0
         if el >= budget_s or n >= cfg.batch:
@@ -353,29 +368,38 @@ def cpu_baseline(cfg, params, x, budget_s=12.0):
 
 
 def run_reference(args):
+    """The reference arm: silarray's own CPU path (oracle/_ref, built from the
+    reference sources) on the host cores, rank 0 only.  One step = one whole
+    512-token sequence of the batch (a bounded sample of the workload, ~0.4 s
+    on 16 cores); W untimed warm-up steps, then K timed steps; the value is
+    tokens processed / wall time of the K steps."""
+    import oracle as O
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
     from silarray_b200 import transformer
-    cfg = transformer.Config()
-    params = transformer.init_params(cfg, seed=0)
-    x = transformer.init_input(cfg, seed=1)
-    vals = []
-    for _ in range(args.warmup):
-        pass  # the CPU path has no warm-up state worth priming beyond the first sample
-    for _ in range(max(1, args.steps)):
-        cb = cpu_baseline(cfg, params, x, budget_s=max(2.0, 60.0 / max(1, args.steps)))
-        vals.append(cb["value"])
-    v = sum(vals) / len(vals)
-    cb["value"] = v
+    full = transformer.Config()
+    params = transformer.init_params(full, seed=0)
+    x = transformer.init_input(full, seed=1)
+    one = transformer.Config(batch=1, seq=full.seq, d_model=full.d_model, heads=full.heads, d_ff=full.d_ff)
+    for k in range(args.warmup):
+        _reference_sequence(one, params, x, k)
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        _reference_sequence(one, params, x, args.warmup + k)
+    el = time.perf_counter() - t0
+    v = args.steps * full.seq / el
+    cores = int(os.environ["OPENBLAS_NUM_THREADS"])
+    cb = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "reference" if O.ref is not None else "port",
+          "sample": f"one {full.seq}-token sequence of the batch-{full.batch} workload per step, {args.steps} "
+                    f"timed steps in {el:.1f} s; cblas_sgemm on {cores} threads, other ops single-threaded as "
+                    f"in the reference"}
     line = {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": cfg.tokens / v * 1e3, "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": full.tokens / v * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "impl": "reference", "config": {"workload": "transformer_block_fwd", "global_batch": cfg.batch,
-                                            "seq_len": cfg.seq, "d_model": cfg.d_model, "heads": cfg.heads,
-                                            "d_ff": cfg.d_ff, "parallelism": "cpu"},
-            "cpu_baseline": cb, "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                                        "d2h_bytes_per_step": 0}}
+            "impl": "reference", "config": workload_config(full, world),
+            "timed_region_s": el, "cpu_baseline": cb,
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -527,10 +551,8 @@ def run_ours(args):
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "transformer_block_fwd", "global_batch": full.batch, "seq_len": full.seq,
-                       "d_model": full.d_model, "heads": full.heads, "d_ff": full.d_ff,
-                       "parallelism": f"dp{world}", "l2": "flushed (256 MiB write) before every timed step",
-                       "launch": "CUDA-graph replay of the forward's kernels (captured after its first eager run)"},
+            "config": workload_config(full, world),
+            "timing": {"launch": "CUDA-graph replay of the forward's kernels (captured after its first eager run)"},
             "clocks": clocks, "e2e": e2e, "gpu_launches": int(launches), "roofline": roofline,
             "sgemm_8192": sg, "cpu_baseline": cpu,
         }

@@ -131,10 +131,11 @@ silcu_status silcu_sum_f32(const float *in, size_t n, float *out, void *workspac
  * device memory (code running inside an allocator or memory-pool callback, or
  * a plugin whose host forbids cudaMalloc after start-up).  Scratch is a fixed
  * 32 KiB array inside the library (4096 fp64 partials) on every GPU that
- * loads it; inputs needing more partials are rejected with SILCU_UNSUPPORTED.
- * The first call on a device looks up that array's address (make it before
- * any stream capture).  All calls share the array: calls that overlap on the
- * GPU (different streams, no ordering between them) race. */
+ * loads it; the first pass never uses more than 4096 CTAs, so every input
+ * size fits.  The first call on a device looks up that array's address (make
+ * it before any stream capture); the address is cached for the process and
+ * does not survive a cudaDeviceReset.  All calls share the array: calls that
+ * overlap on the GPU (different streams, no ordering between them) race. */
 silcu_status silcu_sum_f32_noalloc(const float *in, size_t n, float *out, silcu_stream stream);
 silcu_status silcu_min_f32(const float *in, size_t n, float *out, void *workspace, size_t workspace_bytes, silcu_stream stream);
 silcu_status silcu_max_f32(const float *in, size_t n, float *out, void *workspace, size_t workspace_bytes, silcu_stream stream);

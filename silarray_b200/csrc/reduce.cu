@@ -10,6 +10,7 @@
 // or, for rows of 4K-32K columns, the row in shared memory by one bulk copy
 // per CTA), so softmax and layer_norm read HBM once and write once (the
 // reference reads the row 2-3 times: include/gpu_kernels.metal:1316-1467).
+#include <atomic>
 #include <stdlib.h>
 #include <cooperative_groups.h>
 #include <float.h>
@@ -424,8 +425,10 @@ __global__ void __launch_bounds__(NT) row_smem_kernel(const RowArgs a) {
   // memory: arrive now, wait just before the first exchange.
   if constexpr (CL > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   __syncthreads();
-  // A failed wait (error word set) computes on whatever is in shared memory;
-  // the host reads the status.  Every thread waits, so none reads early.
+  // A failed wait (error word set) computes on whatever is in shared memory
+  // and the copy may still land later: after SILCU_TIMEOUT the outputs are
+  // undefined and the caller must treat the device as failed (the host reads
+  // the status).  Every thread waits, so none reads early.
   tc::mbar_wait(bar, 0, a.err, 41);
   bool started = false;
   // Cluster exchange, push form: every CTA writes its partial into slot
@@ -1122,28 +1125,34 @@ namespace {
 // every GPU that loads this library until the process exits.
 constexpr int kNoAllocPartials = 4096;
 static __device__ __align__(256) double g_noalloc_partials[kNoAllocPartials];
+static_assert(kNoAllocPartials >= kMaxPartials, "the first pass never needs more partials than the scratch holds");
 
 // Host code must not pass the symbol itself to a kernel (on the host it is a
 // stand-in, not a device address); look the address up once per device.
+// The cached address belongs to the device's current context: it does not
+// survive a cudaDeviceReset.  Two host threads making their first call at
+// once both look it up and store the same value (atomic stores).
 double *noalloc_partials(silcu_status *st) {
-  static double *cached[64] = {nullptr};
+  static std::atomic<double *> cached[64];
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess || dev < 0 || dev >= 64) {
     *st = fail(SILCU_CUDA_ERROR, "sum_f32_noalloc: no current device");
     return nullptr;
   }
-  if (!cached[dev]) {
+  double *have = cached[dev].load(std::memory_order_acquire);
+  if (!have) {
     void *p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_partials);
     if (e != cudaSuccess) {
       *st = fail(SILCU_CUDA_ERROR, "sum_f32_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
       return nullptr;
     }
-    cached[dev] = static_cast<double *>(p);
+    have = static_cast<double *>(p);
+    cached[dev].store(have, std::memory_order_release);
   }
   *st = SILCU_OK;
-  return cached[dev];
+  return have;
 }
 
 }  // namespace
@@ -1156,10 +1165,7 @@ extern "C" silcu_status silcu_sum_f32_noalloc(const float *in, size_t n, float *
     sum_seq_small<<<1, 256, 0, as_stream(stream)>>>(in, int(n), out);
     return check_launch("sum_f32_noalloc");
   }
-  const int g = red_grid(n);
-  if (g > kNoAllocPartials)
-    return fail(SILCU_UNSUPPORTED, "sum_f32_noalloc: needs %d partials, the built-in scratch holds %d", g,
-                kNoAllocPartials);
+  const int g = red_grid(n);  // at most kMaxPartials <= kNoAllocPartials (static_assert above)
   silcu_status st;
   double *part = noalloc_partials(&st);
   if (!part) return st;

@@ -263,7 +263,11 @@ class Block:
                 self._forward_seqs(x, out, b0, nb)
             n = gpu.lib().silcu_kernel_launches() - n0
             if len(self._graph_cache) >= self.MAX_GRAPHS:  # bounded: drop the oldest capture
-                self._graph_cache.pop(next(iter(self._graph_cache)))
+                old = self._graph_cache.pop(next(iter(self._graph_cache)))
+                # the dropped graph's workspace may be its last reference: a replay of it
+                # may still run on this stream, so free it only after the stream's work
+                if old[2] is not None:
+                    old[2].record_stream(torch.cuda.current_stream(self.dev))
             self._graph_cache[key] = (graph, n, gpu.workspace(0, self.dev))
             return
         g[0].replay()
@@ -294,52 +298,3 @@ class Block:
         gpu.layer_norm_split(r1, self.g2, self.be2, T, d, cfg.eps, *h)
         gpu.gemm(h, self.w1_t, M=T, N=f, K=d, trans_b=True, bias=self.b1, act="relu", no_c=True, C_split=ff)
         gpu.gemm(ff, self.w2_t, outs, M=T, N=d, K=f, trans_b=True, bias=self.b2, residual=r1)
-
-
-def reference_forward(cfg, params, x):
-    """CPU reference of the same block: the reference's own CPU build when it
-    is present (oracle/_ref, every op a sil:: array op), else the oracle
-    restatement composed the same way.  Test infrastructure only."""
-    import oracle as O
-    if O.ref is not None:
-        return O.ref.transformer_block(x, cfg.batch, cfg.seq, cfg.d_model, cfg.heads, cfg.d_ff, params)
-    return _restated_forward(cfg, params, x)
-
-
-def _restated_forward(cfg, p, x):
-    import oracle as O
-    S, d, H, hd = cfg.seq, cfg.d_model, cfg.heads, cfg.head_dim
-    scale = np.float32(1.0) / np.sqrt(np.float32(hd))
-    out = np.empty_like(x)
-    lin = lambda a, w, b: O.binary("add", O.sgemm(a, w), b).reshape(a.shape[0], w.shape[1])  # noqa: E731
-    for bi in range(cfg.batch):
-        X = x[bi * S:(bi + 1) * S]
-        h = O.layer_norm(X, p["g1"], p["be1"])
-        Q, K, V = lin(h, p["wq"], p["bq"]), lin(h, p["wk"], p["bk"]), lin(h, p["wv"], p["bv"])
-        ctx = np.empty((S, d), np.float32)
-        for hh in range(H):
-            sl = slice(hh * hd, (hh + 1) * hd)
-            q, k, v = (np.ascontiguousarray(m[:, sl]) for m in (Q, K, V))
-            sc = O.scalar_op("mul", scale, O.sgemm(q, k, tb=True)).reshape(S, S)
-            at = O.softmax(sc)
-            ctx[:, sl] = O.sgemm(at, v)
-        r1 = O.binary("add", X, lin(ctx, p["wo"], p["bo"])).reshape(S, d)
-        h2 = O.layer_norm(r1, p["g2"], p["be2"])
-        ff = O.relu(lin(h2, p["w1"], p["b1"]))
-        out[bi * S:(bi + 1) * S] = O.binary("add", r1, lin(ff, p["w2"], p["b2"])).reshape(S, d)
-    return out
-
-
-def check_parity(got, ref, cfg):
-    """End-to-end tolerance for the 6-GEMM chain: |g - r| <= 2e-4 * (1 + |r|)
-    (each GEMM is within sqrt(K) * (1e-6 + 1e-5|r|) of the oracle; layer_norm
-    and softmax amplify the differences by O(1) factors)."""
-    got = np.asarray(got, np.float64).reshape(ref.shape)
-    ref = np.asarray(ref, np.float64)
-    err = np.abs(got - ref)
-    lim = 2e-4 * (1.0 + np.abs(ref))
-    if not (err <= lim).all():
-        i = int(np.argmax(err - lim))
-        raise AssertionError(f"transformer parity: {(err > lim).sum()} of {err.size} outside; worst "
-                             f"got {got.ravel()[i]!r} ref {ref.ravel()[i]!r}; max err {err.max():.3e}")
-    return float(err.max())

@@ -62,9 +62,15 @@ def test_sum_i32_wraps(cuda):
                                        (2, 40000), (2, 40001), (1000, 8192), (700, 16384), (600, 32768),
                                        (301, 8256)])
 def test_row_ops(cuda, rows, cols):
-    """Row ops against the oracle.  Rows of 4K-32K columns (multiples of 64)
-    run on a persistent grid where each CTA / cluster prefetches its next
-    row; the many-row cases give every CTA several rows."""
+    """Row ops against the oracle.  Rows up to 4096 columns run from
+    registers (a warp or a CTA per row); softmax / layer_norm / argmax on
+    rows of 4K-32K columns (multiples of 64) run one CTA per row (up to 8192)
+    or one 2-CTA cluster per row from shared memory; the row sum keeps the row
+    in registers across a 4-CTA cluster; other widths take the generic loop."""
+    _check_row_ops(rows, cols)
+
+
+def _check_row_ops(rows, cols):
     rng = np.random.default_rng(rows * 100003 + cols)
     x = rng.normal(0, 2, (rows, cols)).astype(np.float32)
     X = dev(x)
@@ -86,6 +92,33 @@ def test_row_ops(cuda, rows, cols):
     s0 = host(gpu.sum_axis0_f32(X))
     for c in range(0, cols, max(1, cols // 50)):
         assert_sum_close(s0[c], x[:, c], what=f"sum(axis=0) col {c}")
+
+
+_VARIANT_SHAPES = [(3, 8256), (5, 16384), (3, 32768), (600, 32768)]
+
+
+def run_row_variant(env):
+    """Runs the long-row cases in a fresh process (the implementation
+    switches are read once per process) with `env` set; used by the test
+    below and as a script: python -m tests.test_gpu_reduce VAR=VALUE."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = ("import sys; sys.path.insert(0, %r); from tests import test_gpu_reduce as T; "
+            "[T._check_row_ops(r, c) for r, c in T._VARIANT_SHAPES]; print('variant ok')" % root)
+    r = subprocess.run([sys.executable, "-c", code], env={**os.environ, **env}, capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0 and "variant ok" in r.stdout, r.stdout[-2000:] + r.stderr[-3000:]
+
+
+@pytest.mark.parametrize("env", [{"SILCU_ROW_SMEM_CL": "4"}, {"SILCU_ROW_IMPL": "0"}, {"SILCU_ROW_IMPL": "1"}],
+                         ids=["smem-cluster4", "register-rows", "smem-rowsum"])
+def test_row_ops_other_implementations(cuda, env):
+    """The row-op variants the defaults do not select: the 4-CTA shared-memory
+    cluster above 8K columns, the register-resident long-row kernels
+    (clusters of 4) for every op, and the shared-memory row sum."""
+    run_row_variant(env)
 
 
 def test_argmax_ties_and_floor_rows(cuda):

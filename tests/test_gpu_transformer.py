@@ -6,6 +6,7 @@ import pytest
 import torch
 
 from silarray_b200 import gpu, transformer
+from oracle import transformer_ref as TR
 
 pytestmark = pytest.mark.gpu
 
@@ -20,8 +21,8 @@ def test_block_forward(cuda, cfg):
     blk = transformer.Block(cfg, p, device="cuda")
     out = blk.forward(torch.from_numpy(x).cuda())
     torch.cuda.synchronize()
-    ref = transformer.reference_forward(cfg, p, x)
-    transformer.check_parity(out.cpu().numpy(), ref, cfg)
+    ref = TR.reference_forward(cfg, p, x)
+    TR.check_parity(out.cpu().numpy(), ref, cfg)
     gpu.device_status()
 
 

@@ -162,11 +162,14 @@ def test_affine_fold_large_path_uses_fma():
     np.testing.assert_array_equal(O.scalar_op("sub", 1.5, x, left=True), R.scalar_chain(x, [("sub", 1.5, True)]))
 
 
-@pytest.mark.skipif(not os.path.exists("/root/reference/test/test_array.cpp"),
-                    reason="reference sources not present")
+REF = os.environ.get("SILARRAY_REF", "/root/reference")
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(REF, "test", "test_array.cpp")),
+                    reason="reference sources not present (set SILARRAY_REF)")
 def test_reference_doctest_suite_passes_on_oracle_build():
     root = os.path.dirname(HERE)
-    r = subprocess.run(["make", "-s", "-C", os.path.join(root, "oracle"), "check-ref"],
+    r = subprocess.run(["make", "-s", "-C", os.path.join(root, "oracle"), f"REF={REF}", "check-ref"],
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
     assert "Status: SUCCESS" in r.stdout

