@@ -411,22 +411,22 @@ def run_ours(args):
     import torch.distributed as dist
 
     from silarray_b200 import _lib, gpu, transformer
+    from silarray_b200 import dist as sd
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        sd.init("nccl", timeout_s=300, device=dev)
     lib = _lib.lib()
 
     full = transformer.Config()
-    if full.batch % world:
-        raise SystemExit(f"global batch {full.batch} does not split over {world} ranks")
-    cfg = transformer.Config(batch=full.batch // world)
-    params = transformer.init_params(cfg, seed=0)
+    params = transformer.init_params(full, seed=0)
     x_all = transformer.init_input(full, seed=1)
-    x_local = np.ascontiguousarray(x_all[rank * cfg.tokens:(rank + 1) * cfg.tokens])
-    blk = transformer.Block(cfg, params, device=dev)
+    shard = sd.ShardedBlock(full, params, dev, rank=rank, world=world)  # this rank's sequences of the batch
+    cfg, blk = shard.local, shard.block
+    t0, t1 = shard.token_span
+    x_local = np.ascontiguousarray(x_all[t0:t1])
     x_dev = torch.from_numpy(x_local).to(dev)
     out = torch.empty(cfg.tokens * cfg.d_model, dtype=torch.float32, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)

@@ -40,14 +40,17 @@ def _restated_forward(cfg, p, x):
     return out
 
 
+BLOCK_TOL = 2e-5  # |g - r| <= BLOCK_TOL * (1 + |r|) end to end; measured worst 4.1e-6 at the bench shape
+
+
 def check_parity(got, ref, cfg):
-    """End-to-end tolerance for the 6-GEMM chain: |g - r| <= 2e-4 * (1 + |r|)
+    """End-to-end tolerance for the 6-GEMM chain: |g - r| <= BLOCK_TOL * (1 + |r|)
     (each GEMM is within sqrt(K) * (1e-6 + 1e-5|r|) of the oracle; layer_norm
     and softmax amplify the differences by O(1) factors)."""
     got = np.asarray(got, np.float64).reshape(ref.shape)
     ref = np.asarray(ref, np.float64)
     err = np.abs(got - ref)
-    lim = 2e-4 * (1.0 + np.abs(ref))
+    lim = BLOCK_TOL * (1.0 + np.abs(ref))
     if not (err <= lim).all():
         i = int(np.argmax(err - lim))
         raise AssertionError(f"transformer parity: {(err > lim).sum()} of {err.size} outside; worst "

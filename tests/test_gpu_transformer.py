@@ -1,6 +1,6 @@
 """Transformer block forward on the GPU vs the reference CPU build of the same
 graph (oracle/_ref: every op a sil:: array op on Device::CPU), end-to-end
-tolerance |g - r| <= 2e-4 (1 + |r|)."""
+tolerance |g - r| <= 2e-5 (1 + |r|)."""
 import numpy as np
 import pytest
 import torch
