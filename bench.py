@@ -40,9 +40,10 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sgemm", action="store_true", help="skip the 8192^3 SGEMM side measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-suite", action="store_true", help="skip the per-configuration suite in the headline line")
     ap.add_argument("--suite", action="store_true",
                     help="measure every configuration of the metric (one JSON line each) instead of the headline")
-    ap.add_argument("--profile-case", default=None, choices=["gemm", "block", "attention", "hbm"],
+    ap.add_argument("--profile-case", default=None, choices=["gemm", "block", "attention", "hbm", "sgemm"],
                     help="run only a small case for ncu: the FFN-up GEMM of the workload, or a 2-sequence block")
     return ap.parse_args()
 
@@ -67,8 +68,9 @@ def profile_case(args):
     on the device) warmup+1 times; `block` runs a 2-sequence transformer forward;
     `attention` the fused attention on a quarter of the BMM-attention config;
     `hbm` the HBM-bound kernels of the suite once each after the warm-ups
-    (GEMV 1x4096.4096x4096, softmax / layer_norm 4096x8192 and 4096x32768,
-    argmax 4096x32768, global sum 2^28: ~2.5 GB on the device)."""
+    (GEMV 1x4096.4096x4096, small batch 32x4096.4096x768, softmax /
+    layer_norm 4096x8192 and 4096x32768, argmax 4096x32768, global sum 2^28:
+    ~2.5 GB on the device); `sgemm` the 8192^3 SGEMM (~1 GB)."""
     import torch
     from silarray_b200 import gpu, transformer
     dev = torch.device("cuda", 0)
@@ -86,6 +88,14 @@ def profile_case(args):
         for _ in range(args.warmup + 1):
             gpu.attention(qs, ks, vt, Sq=S, Sk=S, batch=BH, heads=1, ldq=d, sq_b=S * d, sq_h=S * d, ldk=d,
                           sk_b=S * d, sk_h=S * d, ldv=S, sv_b=d * S, sv_h=d * S, scale=0.125, O=Ob)
+    elif args.profile_case == "sgemm":
+        n = 8192  # the metric's SGEMM, plain fp32 operands (split pre-pass + tc_gemm), ~1 GB on the device
+        g = torch.Generator(device=dev).manual_seed(0)
+        Aa = torch.rand(n * n, device=dev, generator=g) * 2 - 1
+        Bb = torch.rand(n * n, device=dev, generator=g) * 2 - 1
+        Cc = torch.empty(n * n, device=dev)
+        for _ in range(args.warmup + 1):
+            gpu.gemm(Aa, Bb, Cc, M=n, N=n, K=n)
     elif args.profile_case == "hbm":
         g = torch.Generator(device=dev).manual_seed(0)
         x, W, bb, y = (torch.randn(4096, device=dev, generator=g), torch.randn(4096 * 4096, device=dev, generator=g),
@@ -95,8 +105,11 @@ def profile_case(args):
         o32 = torch.empty_like(r32)
         gm, bt = torch.ones(32768, device=dev), torch.zeros(32768, device=dev)
         flat = torch.rand(1 << 28, device=dev, generator=g) * 2 - 1
+        X32, W32, Y32 = (torch.randn(32 * 4096, device=dev, generator=g), torch.randn(4096 * 768, device=dev, generator=g),
+                         torch.empty(32 * 768, device=dev))
         for _ in range(args.warmup + 1):
             gpu.sgemv(x, W, y, 4096, 4096, bias=bb)
+            gpu.gemm(X32, W32, Y32, M=32, N=768, K=4096)
             gpu.softmax(r8, o32[: r8.numel()], rows=4096, cols=8192)
             gpu.layer_norm(r8, o32[: r8.numel()], gamma=gm[:8192], beta=bt[:8192], rows=4096, cols=8192)
             gpu.softmax(r32, o32, rows=4096, cols=32768)
@@ -115,10 +128,11 @@ def profile_case(args):
     return 0
 
 
-def run_suite(args):
+def run_suite(args, sink=None):
     """Every configuration of BASELINE.json's metric on one GPU: algorithmic
     bytes or FLOPs per call / CUDA-event time (L2 flushed before each timed
-    call), against the measured HBM copy bandwidth or the 3xTF32 ceiling."""
+    call), against the measured HBM copy bandwidth or the 3xTF32 ceiling.
+    Prints one JSON line per configuration, or appends them to `sink`."""
     import numpy as np
     import torch
     from silarray_b200 import gpu
@@ -180,7 +194,10 @@ def run_suite(args):
         if flops is not None:
             line.update({"TFLOP/s": flops / sec / 1e12, "frac_of_3xtf32_ceiling": flops / sec / 1e12 / ceiling})
         line.update(extra)
-        print(json.dumps(line), flush=True)
+        if sink is not None:
+            sink.append(line)
+        else:
+            print(json.dumps(line), flush=True)
 
     U = lambda *sh: torch.rand(*sh, device=dev, generator=g) * 2 - 1  # noqa: E731
     Nn = lambda std, *sh: torch.randn(*sh, device=dev, generator=g) * std  # noqa: E731
@@ -547,6 +564,13 @@ def run_ours(args):
         cpu = None
         if not args.no_cpu and world == 1:
             cpu = cpu_baseline(cfg, params, x_local, budget_s=12.0)
+        suite = None
+        if not args.no_suite and world == 1:
+            # every other configuration of the metric, one entry each (~15 s)
+            del gargs
+            torch.cuda.empty_cache()
+            suite = []
+            run_suite(argparse.Namespace(steps=5, warmup=3), sink=suite)
         result = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
@@ -554,7 +578,7 @@ def run_ours(args):
             "config": workload_config(full, world),
             "timing": {"launch": "CUDA-graph replay of the forward's kernels (captured after its first eager run)"},
             "clocks": clocks, "e2e": e2e, "gpu_launches": int(launches), "roofline": roofline,
-            "sgemm_8192": sg, "cpu_baseline": cpu,
+            "sgemm_8192": sg, "cpu_baseline": cpu, "suite": suite,
         }
         print(json.dumps(result), flush=True)
     if world > 1:
