@@ -4,9 +4,21 @@
 // names, arguments and meaning (reference include/gpu.h:266-1036), and runs
 // each through the C ABI of include/silcu.h (libsilcu.so, sm_100a kernels):
 // a storage handle becomes `(float *)data + off` and its `len`.  Work is
-// queued on CUDA's legacy default stream; gpu_context::flush() waits for it,
-// as the reference's command-buffer commit/wait does (gpu.h:107-123).  Errors
-// surface as std::runtime_error with the library's message.
+// queued on one non-blocking stream per process; gpu_context::flush() waits
+// for it, as the reference's command-buffer commit/wait does (gpu.h:107-123).
+// Errors surface as std::runtime_error with the library's message.
+//
+// Chain fusion: the evaluator (include/array.h:1987-2061) calls one gpu::
+// function per node.  Consecutive fp32 elementwise calls over the same
+// element count (add/sub/mul/div/pow with storage-length broadcasting,
+// sigmoid, relu, sigmoid_backward, the folded affine) are not launched one
+// by one: they queue as a chain, and the chain runs as ONE fused kernel
+// (silcu_fused_multi_f32) when anything else needs the device or the host
+// reads (flush).  A node's result is written only if its storage is still
+// referenced outside the chain when the chain runs (a user array or a later
+// node holds it); intermediates nobody can read never reach HBM.  Every
+// instruction rounds like the node it replaces, so results are those of the
+// node-by-node evaluation bit for bit.
 //
 // The host layer owns the only allocations: managed storage (unified_memory.h)
 // and one growing device workspace for the multi-pass kernels.
@@ -21,6 +33,7 @@
 #include <stdexcept>
 #include <string>
 #include <type_traits>
+#include <vector>
 
 #include "silcu.h"
 
@@ -32,7 +45,17 @@ inline void check(silcu_status st) {
   if (st != SILCU_OK) throw std::runtime_error(std::string("silarray b200: ") + silcu_last_error());
 }
 
-inline silcu_stream stream() { return nullptr; }  // legacy default stream
+// The process's work stream (non-blocking: it does not serialise with the
+// legacy default stream other libraries may use), created on first use.
+inline silcu_stream stream() {
+  static cudaStream_t s = [] {
+    cudaStream_t t = nullptr;
+    if (cudaStreamCreateWithFlags(&t, cudaStreamNonBlocking) != cudaSuccess)
+      throw std::runtime_error("silarray b200: cannot create the work stream");
+    return t;
+  }();
+  return reinterpret_cast<silcu_stream>(s);
+}
 
 // Device workspace for multi-pass kernels, grown on demand.  Growth waits for
 // queued work first, since kernels in flight may still use the old buffer.
@@ -42,7 +65,7 @@ inline void *workspace(size_t bytes) {
   if (bytes == 0) return ptr;
   if (bytes > cap) {
     if (ptr) {
-      cudaStreamSynchronize(nullptr);
+      cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream()));
       cudaFree(ptr);
     }
     size_t want = bytes + bytes / 4 + (1u << 20);
@@ -62,6 +85,223 @@ template <class T>
 inline T *ptr(const storage &s) {
   return static_cast<T *>(s.data) + s.off;
 }
+
+// ------------------------------------------------------------ chain fusion
+struct chain_node {
+  int op = 0;  // silcu_opcode of the node (ADD .. RDIV_IMM)
+  storage out;
+  storage in[2];
+  int nin = 0;
+  float imm0 = 0.0f, imm1 = 0.0f;
+};
+
+inline bool same_view(const storage &a, const storage &b) {
+  return a.data == b.data && a.off == b.off && a.len == b.len;
+}
+
+inline silcu_status run_single(const chain_node &c) {
+  auto in0 = ptr<const float>(c.in[0]);
+  auto o = ptr<float>(c.out);
+  const size_t n = c.out.len;
+  switch (c.op) {
+    case SILCU_OP_ADD: return silcu_add_f32(in0, c.in[0].len, ptr<const float>(c.in[1]), c.in[1].len, o, n, stream());
+    case SILCU_OP_SUB: return silcu_sub_f32(in0, c.in[0].len, ptr<const float>(c.in[1]), c.in[1].len, o, n, stream());
+    case SILCU_OP_MUL: return silcu_mul_f32(in0, c.in[0].len, ptr<const float>(c.in[1]), c.in[1].len, o, n, stream());
+    case SILCU_OP_DIV: return silcu_div_f32(in0, c.in[0].len, ptr<const float>(c.in[1]), c.in[1].len, o, n, stream());
+    case SILCU_OP_POW: return silcu_pow_f32(in0, c.in[0].len, ptr<const float>(c.in[1]), c.in[1].len, o, n, stream());
+    case SILCU_OP_SIGMOID: return silcu_sigmoid_f32(in0, o, n, stream());
+    case SILCU_OP_RELU: return silcu_relu_f32(in0, o, n, stream());
+    case SILCU_OP_SIGMOID_BWD: return silcu_sigmoid_backward_f32(in0, ptr<const float>(c.in[1]), o, n, stream());
+    case SILCU_OP_AFFINE: return silcu_affine_f32(in0, o, n, c.imm0, c.imm1, 0, stream());
+    case SILCU_OP_AFFINE_FMA: return silcu_affine_f32(in0, o, n, c.imm0, c.imm1, 1, stream());
+    default: return SILCU_INVALID_ARGUMENT;
+  }
+}
+
+// Pending chain of elementwise nodes (one per process; the API is
+// single-threaded like the reference's).
+class chain {
+ public:
+  static chain &instance() {
+    static chain c;
+    return c;
+  }
+
+  // Queues `out = op(a[, b])`; n = out.len elements.
+  void push(int op, const storage &out, const storage *a, const storage *b, float imm0 = 0.0f,
+            float imm1 = 0.0f) {
+    if (!nodes_.empty() && !fits_(out, a, b)) run();
+    chain_node c;
+    c.op = op;
+    c.out = out;
+    c.in[0] = *a;
+    c.nin = 1;
+    if (b) {
+      c.in[1] = *b;
+      c.nin = 2;
+    }
+    c.imm0 = imm0;
+    c.imm1 = imm1;
+    nodes_.push_back(std::move(c));
+    gpu_pending_ = true;
+  }
+
+  // Launches the pending chain (one kernel) and forgets it.
+  void run() {
+    if (nodes_.empty()) return;
+    std::vector<chain_node> nodes;
+    nodes.swap(nodes_);
+    if (nodes.size() == 1) {
+      check(run_single(nodes[0]));
+      return;
+    }
+    if (!run_fused_(nodes))
+      for (auto &c : nodes) check(run_single(c));
+  }
+
+  size_t pending() const { return nodes_.size(); }
+
+ private:
+  static constexpr size_t kMaxNodes = 12;
+
+  int producer_(const storage &x, size_t upto) const {
+    for (size_t j = upto; j-- > 0;)
+      if (same_view(nodes_[j].out, x)) return int(j);
+    return -1;
+  }
+
+  // May the node join the chain?  Same element count; operands either a
+  // chain result viewed whole or memory no chain node writes; the output no
+  // chain operand's memory; at most SILCU_MAX_INPUTS distinct outside inputs.
+  bool fits_(const storage &out, const storage *a, const storage *b) const {
+    if (nodes_.size() >= kMaxNodes || out.len != nodes_[0].out.len) return false;
+    const storage *ops[2] = {a, b};
+    std::vector<const void *> ext;
+    for (auto &c : nodes_) {
+      if (c.out.data == out.data) return false;
+      for (int i = 0; i < c.nin; i++) {
+        if (c.in[i].data == out.data) return false;
+        if (producer_(c.in[i], nodes_.size()) < 0) ext.push_back(c.in[i].data);
+      }
+    }
+    for (const storage *x : ops) {
+      if (!x) continue;
+      if (producer_(*x, nodes_.size()) >= 0) continue;
+      for (auto &c : nodes_)
+        if (c.out.data == x->data) return false;  // a partial view of a chain result
+      ext.push_back(x->data);
+    }
+    std::vector<const void *> uniq;
+    for (auto p : ext) {
+      bool seen = false;
+      for (auto q : uniq) seen = seen || q == p;
+      if (!seen) uniq.push_back(p);
+    }
+    return uniq.size() <= SILCU_MAX_INPUTS;
+  }
+
+  // One fused_multi launch for the chain; false if it does not fit the
+  // interpreter (registers, outputs), in which case nothing was launched.
+  bool run_fused_(const std::vector<chain_node> &nodes) {
+    const size_t n = nodes[0].out.len;
+    const size_t N = nodes.size();
+    // Liveness: a result must be stored if anything besides this chain still
+    // holds its buffer.
+    std::vector<bool> live(N, true);
+    for (size_t k = 0; k + 1 < N; k++) {
+      const void *key = nodes[k].out.buf.get();
+      long held = 0;
+      for (auto &c : nodes) {
+        held += c.out.buf.get() == key;
+        for (int i = 0; i < c.nin; i++) held += c.in[i].buf.get() == key;
+      }
+      live[k] = nodes[k].out.buf.use_count() > held;
+    }
+    auto producer = [&](const storage &x, size_t upto) {
+      for (size_t j = upto; j-- > 0;)
+        if (same_view(nodes[j].out, x)) return int(j);
+      return -1;
+    };
+    // last reader of each result
+    std::vector<int> last_use(N, -1);
+    for (size_t k = 0; k < N; k++)
+      for (int i = 0; i < nodes[k].nin; i++) {
+        int j = producer(nodes[k].in[i], k);
+        if (j >= 0) last_use[j] = int(k);
+      }
+    silcu_program prog{};
+    const float *inputs[SILCU_MAX_INPUTS];
+    size_t lens[SILCU_MAX_INPUTS];
+    float *outs[SILCU_MAX_OUTPUTS];
+    int n_in = 0, n_out = 0;
+    std::vector<const storage *> in_st;
+    bool busy[8] = {false};
+    std::vector<int> reg_of(N, -1);
+    auto alloc = [&]() {
+      for (int r = 0; r < 8; r++)
+        if (!busy[r]) {
+          busy[r] = true;
+          return r;
+        }
+      return -1;
+    };
+    auto emit = [&](int op, int dst, int a, int b, float i0, float i1) {
+      if (prog.n_instr >= SILCU_MAX_PROGRAM) return false;
+      prog.code[prog.n_instr++] = silcu_instr{op, dst, a, b, i0, i1};
+      return true;
+    };
+    for (size_t k = 0; k < N; k++) {
+      const chain_node &c = nodes[k];
+      int src[2] = {0, 0};
+      int temp[2] = {-1, -1};
+      for (int i = 0; i < c.nin; i++) {
+        int j = producer(c.in[i], k);
+        if (j >= 0) {
+          src[i] = reg_of[j];
+          continue;
+        }
+        int slot = -1;
+        for (int q = 0; q < n_in; q++)
+          if (same_view(*in_st[q], c.in[i])) slot = q;
+        if (slot < 0) {
+          if (n_in >= SILCU_MAX_INPUTS) return false;
+          slot = n_in++;
+          in_st.push_back(&c.in[i]);
+          inputs[slot] = ptr<const float>(c.in[i]);
+          lens[slot] = c.in[i].len;
+        }
+        int r = alloc();
+        if (r < 0 || !emit(SILCU_OP_LOAD, r, slot, 0, 0.0f, 0.0f)) return false;
+        src[i] = temp[i] = r;
+      }
+      // operands whose last reader is this node free their registers first
+      for (int i = 0; i < 2; i++)
+        if (temp[i] >= 0) busy[temp[i]] = false;
+      for (int i = 0; i < c.nin; i++) {
+        int j = producer(c.in[i], k);
+        if (j >= 0 && last_use[j] == int(k)) busy[reg_of[j]] = false;
+      }
+      int dst = alloc();
+      if (dst < 0 || !emit(c.op, dst, src[0], c.nin > 1 ? src[1] : src[0], c.imm0, c.imm1)) return false;
+      reg_of[k] = dst;
+      if (live[k]) {
+        if (n_out >= SILCU_MAX_OUTPUTS) return false;
+        outs[n_out] = ptr<float>(c.out);
+        if (!emit(SILCU_OP_STORE, 0, dst, n_out, 0.0f, 0.0f)) return false;
+        n_out++;
+      }
+      if (last_use[k] < 0) busy[dst] = false;
+    }
+    prog.n_inputs = n_in;
+    check(silcu_fused_multi_f32(&prog, inputs, lens, outs, n_out, n, stream()));
+    return true;
+  }
+
+  std::vector<chain_node> nodes_;
+};
+
+// Every launch that is not itself a chain node runs the pending chain first.
+inline void before_launch() { chain::instance().run(); }
 
 inline void queued() { gpu_pending_ = true; }
 
@@ -86,6 +326,7 @@ inline silcu_gemm_args gemm_args(const storage &A, const storage &B, storage &C,
 }
 
 inline void run_gemm(const silcu_gemm_args &a) {
+  before_launch();
   size_t need = silcu_sgemm_workspace_bytes(&a);
   void *ws = workspace(need);
   check(silcu_sgemm_ex(&a, ws, need ? workspace_cap(need) : 0, stream()));
@@ -102,6 +343,7 @@ class gpu_context {
   }
   // Waits for every queued kernel (the reference's commit + waitUntilCompleted).
   void flush() {
+    b200::before_launch();
     b200::check(silcu_synchronize(b200::stream()));
     b200::check(silcu_device_status(b200::stream()));
     gpu_pending_ = false;
@@ -114,16 +356,11 @@ class gpu {
     using b200::ptr;
     silcu_status st;
     if constexpr (std::is_same_v<T, float>) {
-      auto a = ptr<const float>(A), b = ptr<const float>(B);
-      auto o = ptr<float>(OUT);
-      switch (op) {
-        case 0: st = silcu_add_f32(a, A.len, b, B.len, o, OUT.len, b200::stream()); break;
-        case 1: st = silcu_sub_f32(a, A.len, b, B.len, o, OUT.len, b200::stream()); break;
-        case 2: st = silcu_mul_f32(a, A.len, b, B.len, o, OUT.len, b200::stream()); break;
-        case 3: st = silcu_div_f32(a, A.len, b, B.len, o, OUT.len, b200::stream()); break;
-        default: st = silcu_pow_f32(a, A.len, b, B.len, o, OUT.len, b200::stream()); break;
-      }
+      static constexpr int kOp[5] = {SILCU_OP_ADD, SILCU_OP_SUB, SILCU_OP_MUL, SILCU_OP_DIV, SILCU_OP_POW};
+      b200::chain::instance().push(kOp[op], OUT, &A, &B);
+      return;
     } else if constexpr (std::is_same_v<T, int>) {
+      b200::before_launch();
       auto a = ptr<const int32_t>(A), b = ptr<const int32_t>(B);
       auto o = ptr<int32_t>(OUT);
       switch (op) {
@@ -142,6 +379,7 @@ class gpu {
 
   static size_t reduce_(silcu_status (*fn)(const float *, size_t, float *, void *, size_t, silcu_stream),
                         const storage &IN, storage &OUT, size_t length) {
+    b200::before_launch();
     size_t need = silcu_reduce_workspace_bytes(length);
     void *ws = b200::workspace(need);
     b200::check(fn(b200::ptr<const float>(IN), length, b200::ptr<float>(OUT), ws, b200::workspace_cap(need),
@@ -159,14 +397,8 @@ class gpu {
   template <value_type T> static void pow(const storage &A, const storage &B, storage &OUT) { arith_<T>(4, A, B, OUT); }
 
   // include/gpu.h:314-320
-  static void sigmoid(const storage &IN, storage &OUT) {
-    b200::check(silcu_sigmoid_f32(b200::ptr<const float>(IN), b200::ptr<float>(OUT), OUT.len, b200::stream()));
-    b200::queued();
-  }
-  static void relu(const storage &IN, storage &OUT) {
-    b200::check(silcu_relu_f32(b200::ptr<const float>(IN), b200::ptr<float>(OUT), OUT.len, b200::stream()));
-    b200::queued();
-  }
+  static void sigmoid(const storage &IN, storage &OUT) { b200::chain::instance().push(SILCU_OP_SIGMOID, OUT, &IN, nullptr); }
+  static void relu(const storage &IN, storage &OUT) { b200::chain::instance().push(SILCU_OP_RELU, OUT, &IN, nullptr); }
 
   // include/gpu.h:323-354, 409-470: the number of partials the caller must
   // finish on the host; here the device finishes, so it is always one.
@@ -180,6 +412,7 @@ class gpu {
   // include/gpu.h:385-406 (the partial buffer of the two-pass Metal kernel is not needed)
   static void sum_axis0_f32(const storage &IN, storage &OUT, size_t rows, size_t cols, const storage &,
                             size_t, size_t) {
+    b200::before_launch();
     size_t need = silcu_sum_axis_workspace_bytes(1, rows, cols);
     void *ws = b200::workspace(need);
     b200::check(silcu_sum_axis_f32(b200::ptr<const float>(IN), b200::ptr<float>(OUT), 1, rows, cols, ws,
@@ -190,6 +423,7 @@ class gpu {
   // include/gpu.h:473-501
   static void layer_norm(const storage &IN, storage &OUT, const storage &gamma, const storage &beta, uint32_t rows,
                          uint32_t cols, float eps) {
+    b200::before_launch();
     b200::check(silcu_layer_norm_f32(b200::ptr<const float>(IN), b200::ptr<float>(OUT),
                                      b200::ptr<const float>(gamma), b200::ptr<const float>(beta), rows, cols, eps,
                                      b200::stream()));
@@ -250,6 +484,7 @@ class gpu {
 
   // include/gpu.h:890-942
   static void argmax_f32(const storage &IN, storage &OUT, uint32_t rows, uint32_t cols) {
+    b200::before_launch();
     size_t need = silcu_argmax_workspace_bytes(rows, cols);
     void *ws = b200::workspace(need);
     b200::check(silcu_argmax_f32(b200::ptr<const float>(IN), b200::ptr<int32_t>(OUT), rows, cols, ws,
@@ -257,17 +492,24 @@ class gpu {
     b200::queued();
   }
   static void softmax(const storage &IN, storage &OUT, uint32_t rows, uint32_t cols) {
+    b200::before_launch();
     b200::check(silcu_softmax_f32(b200::ptr<const float>(IN), b200::ptr<float>(OUT), rows, cols, b200::stream()));
     b200::queued();
   }
 
   // include/gpu.h:945-1004
   static void sigmoid_backward(const storage &dout, const storage &x, storage &OUT, size_t n) {
+    if (n == OUT.len && x.len >= n && dout.len >= n) {
+      b200::chain::instance().push(SILCU_OP_SIGMOID_BWD, OUT, &dout, &x);
+      return;
+    }
+    b200::before_launch();
     b200::check(silcu_sigmoid_backward_f32(b200::ptr<const float>(dout), b200::ptr<const float>(x),
                                            b200::ptr<float>(OUT), n, b200::stream()));
     b200::queued();
   }
   static void bias_sigmoid(storage &data, const storage &bias, size_t n, size_t cols) {
+    b200::before_launch();
     b200::check(silcu_bias_sigmoid_f32(b200::ptr<float>(data), b200::ptr<const float>(bias), n, cols,
                                        b200::stream()));
     b200::queued();
@@ -276,6 +518,12 @@ class gpu {
   // below 5,000,000 elements and with fmaf above (include/array.h:2003-2015);
   // the same rule keeps GPU and CPU results equal.
   static void affine(const storage &IN, storage &OUT, size_t n, float scale, float offset) {
+    if (n == OUT.len && IN.len >= n) {
+      b200::chain::instance().push(n >= 5000000 ? SILCU_OP_AFFINE_FMA : SILCU_OP_AFFINE, OUT, &IN, nullptr, scale,
+                                   offset);
+      return;
+    }
+    b200::before_launch();
     b200::check(silcu_affine_f32(b200::ptr<const float>(IN), b200::ptr<float>(OUT), n, scale, offset,
                                  n >= 5000000 ? 1 : 0, b200::stream()));
     b200::queued();

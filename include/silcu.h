@@ -95,7 +95,8 @@ typedef enum silcu_opcode {
   SILCU_OP_SIGMOID = 8,
   SILCU_OP_RELU = 9,
   SILCU_OP_SIGMOID_BWD = 10, /* r[dst] = r[a] * s * (1 - s), s = sigmoid(r[b]) */
-  SILCU_OP_RDIV_IMM = 11    /* r[dst] = imm0 / r[a]                         */
+  SILCU_OP_RDIV_IMM = 11,   /* r[dst] = imm0 / r[a]                         */
+  SILCU_OP_STORE = 12       /* outputs[b][i] = r[a] (silcu_fused_multi_f32 only) */
 } silcu_opcode;
 
 typedef struct silcu_instr {
@@ -114,6 +115,15 @@ typedef struct silcu_program {
 /* `prog_host` is read on the host at call time (passed by value to the kernel). */
 silcu_status silcu_fused_f32(const silcu_program *prog_host, const float *const *inputs_host,
                              const size_t *lens_host, float *out, size_t n, silcu_stream stream);
+/* The same interpreter with several outputs of n elements each: STORE
+ * instructions write a register to outputs[b], and nothing is stored
+ * implicitly.  The host layer's chain fusion uses it to write only the nodes
+ * of a chain whose storage is still referenced (include/array.h:1987-2061
+ * writes every node). */
+#define SILCU_MAX_OUTPUTS 4
+silcu_status silcu_fused_multi_f32(const silcu_program *prog_host, const float *const *inputs_host,
+                                   const size_t *lens_host, float *const *outputs_host, int n_outputs, size_t n,
+                                   silcu_stream stream);
 
 /* ------------------------------------------------------------ reductions
  * Whole-array reductions, single pass over HBM plus a one-block finish.

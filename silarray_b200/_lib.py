@@ -80,6 +80,8 @@ _SIGS = {
     "silcu_bias_sigmoid_f32": ([vp, vp, sz, sz, vp], C.c_int),
     "silcu_affine_f32": ([vp, vp, sz, f32, f32, C.c_int, vp], C.c_int),
     "silcu_fused_f32": ([C.POINTER(Program), C.POINTER(vp), C.POINTER(sz), vp, sz, vp], C.c_int),
+    "silcu_fused_multi_f32": ([C.POINTER(Program), C.POINTER(vp), C.POINTER(sz), C.POINTER(vp), C.c_int, sz, vp],
+                              C.c_int),
     "silcu_reduce_workspace_bytes": ([sz], sz),
     "silcu_sum_f32": ([vp, sz, vp, vp, sz, vp], C.c_int),
     "silcu_sum_f32_noalloc": ([vp, sz, vp, vp], C.c_int),

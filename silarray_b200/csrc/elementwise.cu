@@ -199,6 +199,8 @@ struct FusedParams {
   silcu_program prog;
   const float *in[SILCU_MAX_INPUTS];
   uint64_t len[SILCU_MAX_INPUTS];
+  float *outs[SILCU_MAX_OUTPUTS];  // STORE targets
+  int implicit_store;              // 1: the last instruction's dst goes to `out`
 };
 
 constexpr int kRegs = 8;
@@ -219,6 +221,17 @@ __global__ void __launch_bounds__(kThreads) fused_kernel(const __grid_constant__
       const silcu_instr ins = p.prog.code[pc];
       float4 v;
       float *e = &v.x;
+      if (ins.op == SILCU_OP_STORE) {
+        const float4 r = regs[ins.a & (kRegs - 1)][t];
+        float *dst = p.outs[ins.b & (SILCU_MAX_OUTPUTS - 1)];
+        if (cnt == 4 && ((reinterpret_cast<uintptr_t>(dst + i) & 15) == 0)) {
+          *reinterpret_cast<float4 *>(dst + i) = r;
+        } else {
+          const float *rr = &r.x;
+          for (int k = 0; k < cnt; k++) dst[i + k] = rr[k];
+        }
+        continue;
+      }
       if (ins.op == SILCU_OP_LOAD) {
         const float *src = p.in[ins.a];
         const uint64_t L = p.len[ins.a];
@@ -262,6 +275,7 @@ __global__ void __launch_bounds__(kThreads) fused_kernel(const __grid_constant__
       }
       regs[ins.dst & (kRegs - 1)][t] = v;
     }
+    if (!p.implicit_store) continue;
     const float4 res = regs[p.prog.code[last].dst & (kRegs - 1)][t];
     if (cnt == 4 && ((reinterpret_cast<uintptr_t>(out + i) & 15) == 0)) {
       *reinterpret_cast<float4 *>(out + i) = res;
@@ -335,30 +349,54 @@ silcu_status silcu_affine_f32(const float *in, float *out, size_t n, float scale
   return check_launch("affine");
 }
 
-silcu_status silcu_fused_f32(const silcu_program *prog, const float *const *inputs,
-                             const size_t *lens, float *out, size_t n, silcu_stream s) {
+static silcu_status fused_launch(const char *what, const silcu_program *prog, const float *const *inputs,
+                                 const size_t *lens, float *const *outs, int n_outs, float *out, size_t n,
+                                 silcu_stream s) {
   if (n == 0) return SILCU_OK;
-  if (!prog || !out || prog->n_instr <= 0 || prog->n_instr > SILCU_MAX_PROGRAM ||
-      prog->n_inputs < 0 || prog->n_inputs > SILCU_MAX_INPUTS)
-    return fail(SILCU_INVALID_ARGUMENT, "fused: bad program");
+  if (!prog || prog->n_instr <= 0 || prog->n_instr > SILCU_MAX_PROGRAM || prog->n_inputs < 0 ||
+      prog->n_inputs > SILCU_MAX_INPUTS)
+    return fail(SILCU_INVALID_ARGUMENT, "%s: bad program", what);
   FusedParams p;
   memset(&p, 0, sizeof(p));
   p.prog = *prog;
   for (int j = 0; j < prog->n_inputs; j++) {
-    if (!inputs[j] || lens[j] == 0) return fail(SILCU_INVALID_ARGUMENT, "fused: input %d empty", j);
+    if (!inputs[j] || lens[j] == 0) return fail(SILCU_INVALID_ARGUMENT, "%s: input %d empty", what, j);
     p.in[j] = inputs[j];
     p.len[j] = lens[j];
   }
+  for (int j = 0; j < n_outs; j++) {
+    if (!outs[j]) return fail(SILCU_INVALID_ARGUMENT, "%s: output %d is null", what, j);
+    p.outs[j] = outs[j];
+  }
+  p.implicit_store = out != nullptr;
   for (int pc = 0; pc < prog->n_instr; pc++) {
     const silcu_instr &ins = prog->code[pc];
+    if (ins.op == SILCU_OP_STORE) {
+      if (out || ins.a < 0 || ins.a >= kRegs || ins.b < 0 || ins.b >= n_outs)
+        return fail(SILCU_INVALID_ARGUMENT, "%s: bad store %d", what, pc);
+      continue;
+    }
     if (ins.dst < 0 || ins.dst >= kRegs || ins.op < 0 || ins.op > SILCU_OP_RDIV_IMM ||
         (ins.op != SILCU_OP_LOAD && (ins.a < 0 || ins.a >= kRegs || ins.b < 0 || ins.b >= kRegs)))
-      return fail(SILCU_INVALID_ARGUMENT, "fused: bad instruction %d", pc);
+      return fail(SILCU_INVALID_ARGUMENT, "%s: bad instruction %d", what, pc);
     if (ins.op == SILCU_OP_LOAD && (ins.a < 0 || ins.a >= prog->n_inputs))
-      return fail(SILCU_INVALID_ARGUMENT, "fused: instruction %d loads a missing input", pc);
+      return fail(SILCU_INVALID_ARGUMENT, "%s: instruction %d loads a missing input", what, pc);
   }
   fused_kernel<<<grid_for(n), kThreads, 0, as_stream(s)>>>(p, out, n);
-  return check_launch("fused");
+  return check_launch(what);
+}
+
+silcu_status silcu_fused_f32(const silcu_program *prog, const float *const *inputs,
+                             const size_t *lens, float *out, size_t n, silcu_stream s) {
+  if (!out) return fail(SILCU_INVALID_ARGUMENT, "fused: null output");
+  return fused_launch("fused", prog, inputs, lens, nullptr, 0, out, n, s);
+}
+
+silcu_status silcu_fused_multi_f32(const silcu_program *prog, const float *const *inputs, const size_t *lens,
+                                   float *const *outputs, int n_outputs, size_t n, silcu_stream s) {
+  if (n_outputs < 1 || n_outputs > SILCU_MAX_OUTPUTS || !outputs)
+    return fail(SILCU_INVALID_ARGUMENT, "fused_multi: 1..%d outputs", SILCU_MAX_OUTPUTS);
+  return fused_launch("fused_multi", prog, inputs, lens, outputs, n_outputs, nullptr, n, s);
 }
 
 }  // extern "C"

@@ -11,6 +11,23 @@ enum GemmPath { kPathFfma = 0, kPathSkinny = 1, kPathTc = 2 };
 // Which kernel family silcu_sgemm_ex uses for these arguments.
 int gemm_path(const silcu_gemm_args &a);
 
+// Epilogue of the CUDA-core GEMMs: alpha, bias[col % bias_len], activation,
+// residual, in the reference's order.
+struct SkinnyEpi {
+  float alpha;
+  const float *bias;
+  int64_t bias_len;
+  int act;
+  const float *residual;
+  int64_t ldr;
+};
+
+// Skinny GEMM (2 <= M <= 32, plain row-major operands whose rows are
+// 16-byte aligned): one wave of clusters streaming W by bulk copies
+// (skinny.cu).  No workspace.
+bool skinny_bulk_eligible(const silcu_gemm_args &a);
+silcu_status skinny_bulk_run(const silcu_gemm_args &a, const SkinnyEpi &epi, cudaStream_t s);
+
 // Workspace of the 3xTF32 path: the hi/lo split operands, K-major.
 size_t tc_workspace_bytes(const silcu_gemm_args &a);
 silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t ws_bytes, cudaStream_t s);

@@ -95,16 +95,19 @@ class CombineTimeout(RuntimeError):
     left, or never arrived); the process group has been aborted."""
 
 
-def init(backend=None, timeout_s=DEFAULT_DEADLINE_S, device=None):
+def init(backend=None, timeout_s=DEFAULT_DEADLINE_S, device=None, init_method=None, rank=None, world_size=None):
     """One process per GPU: init_process_group from the torchrun environment
-    (RANK / WORLD_SIZE / MASTER_ADDR / MASTER_PORT) with a short collective
-    timeout, so that a lost rank ends the others' collectives with an error.
-    backend: "nccl" when a device is given or CUDA is available, else "gloo"."""
+    (RANK / WORLD_SIZE / MASTER_ADDR / MASTER_PORT), or from init_method /
+    rank / world_size when given, with a short collective timeout, so that a
+    lost rank ends the others' collectives with an error.  backend: "nccl"
+    when a device is given or CUDA is available, else "gloo"."""
     if dist.is_initialized():
         return
     if backend is None:
         backend = "nccl" if (device is not None or torch.cuda.is_available()) else "gloo"
     kw = {"timeout": datetime.timedelta(seconds=timeout_s)}
+    if init_method is not None:
+        kw.update(init_method=init_method, rank=rank, world_size=world_size)
     if backend == "nccl":
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         kw["device_id"] = dev

@@ -146,12 +146,10 @@ def affine(IN, OUT=None, n=None, scale=1.0, offset=0.0, fused=False):
 
 
 OPCODES = {"load": 0, "add": 1, "sub": 2, "mul": 3, "div": 4, "pow": 5, "affine": 6,
-           "affine_fma": 7, "sigmoid": 8, "relu": 9, "sigmoid_bwd": 10, "rdiv_imm": 11}
+           "affine_fma": 7, "sigmoid": 8, "relu": 9, "sigmoid_bwd": 10, "rdiv_imm": 11, "store": 12}
 
 
-def fused(program, inputs, n, OUT=None):
-    """Runs a fused elementwise program: `program` is a list of
-    (op, dst, a, b, imm0, imm1) tuples; `inputs` CUDA float tensors."""
+def _program(program, inputs):
     if len(program) > _lib.MAX_PROGRAM or len(inputs) > _lib.MAX_INPUTS:
         raise ValueError("program or input list too long")
     prog = _lib.Program()
@@ -164,6 +162,24 @@ def fused(program, inputs, n, OUT=None):
         _dev(t, _F32)
     ptrs = (ct.c_void_p * max(1, len(inputs)))(*[t.data_ptr() for t in inputs])
     lens = (ct.c_size_t * max(1, len(inputs)))(*[t.numel() for t in inputs])
+    return prog, ptrs, lens
+
+
+def fused_multi(program, inputs, outputs, n):
+    """A fused elementwise program with explicit ("store", 0, reg, k) writes
+    into outputs[k] (each of n floats)."""
+    prog, ptrs, lens = _program(program, inputs)
+    for t in outputs:
+        _dev(t, _F32)
+    outs = (ct.c_void_p * max(1, len(outputs)))(*[t.data_ptr() for t in outputs])
+    check(lib().silcu_fused_multi_f32(ct.byref(prog), ptrs, lens, outs, len(outputs), n, _stream()))
+    return outputs
+
+
+def fused(program, inputs, n, OUT=None):
+    """Runs a fused elementwise program: `program` is a list of
+    (op, dst, a, b, imm0, imm1) tuples; `inputs` CUDA float tensors."""
+    prog, ptrs, lens = _program(program, inputs)
     if OUT is None:
         OUT = torch.empty(n, dtype=_F32, device=inputs[0].device)
     _dev(OUT, _F32)

@@ -194,7 +194,7 @@ def test_sharded_block_spans():
 
 
 def _failing_worker(rank, world, port, q, deadline):
-    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    sd.init("gloo", timeout_s=30, init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     if rank == world - 1:
         # this rank fails before the combine and leaves without joining it
         q.put((rank, "raised", 0.0))

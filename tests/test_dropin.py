@@ -24,3 +24,16 @@ def test_reference_suite_on_b200(cuda, mode):
     r = subprocess.run(args, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-2000:]
     assert "Status: SUCCESS" in r.stdout
+
+
+def test_chain_fusion_through_sil_api(cuda):
+    """tests/dropin/chain_fusion.cpp: chains of elementwise nodes evaluated
+    through sil:: run as one fused launch (intermediates the caller holds are
+    stored too), equal to the reference CPU path; the binary is built by
+    `make -C oracle dropin`."""
+    path = os.path.join(ROOT, "oracle", "_ref", "chain_fusion_b200")
+    if not os.path.exists(path):
+        pytest.skip("chain fusion program not built (reference sources were absent at build time)")
+    r = subprocess.run([path], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-2000:]
+    assert "PASSED" in r.stdout

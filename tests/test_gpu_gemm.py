@@ -236,3 +236,30 @@ def test_tc_split_last_wave_full_batch(cuda):
     ref = a[rows].astype(np.float64) @ b.astype(np.float64) + bias + res[rows]
     assert_dot_close(got[rows], ref, K, what="split last wave 16384x768x3072")
     gpu.device_status()
+
+
+@pytest.mark.parametrize("M", [2, 5, 16, 17, 32])
+@pytest.mark.parametrize("N,K", [(768, 4096), (772, 2000), (4096, 1024), (64, 64), (128, 16384)])
+def test_skinny_bulk_path(cuda, M, N, K):
+    """2 <= M <= 32 with 16-byte aligned rows (N, K multiples of 4): the
+    one-wave cluster kernel fed by bulk copies (skinny.cu) -- ragged column
+    blocks (772), a K that does not split evenly (2000), one chunk (64) and
+    the longest slices (16384); alpha, bias, sigmoid and a residual in the
+    epilogue; deterministic across calls."""
+    rng = np.random.default_rng(M * 7 + N + K)
+    a = rng.normal(0, 1, (M, K)).astype(np.float32)
+    b = rng.normal(0, 0.02, (K, N)).astype(np.float32)
+    bias = rng.normal(0, 0.1, N).astype(np.float32)
+    res = rng.normal(0, 1, (M, N)).astype(np.float32)
+    got = host(gpu.gemm(dev(a), dev(b), M=M, N=N, K=K, alpha=0.5, bias=dev(bias), act="sigmoid",
+                        residual=dev(res))).reshape(M, N)
+    r = O.scalar_op("mul", np.float32(0.5), O.sgemm(a, b))
+    r = O.sigmoid(O.binary("add", r.ravel(), bias))
+    ref = O.binary("add", r, res.ravel()).reshape(M, N)
+    assert_dot_close(got, ref, K, what=f"skinny bulk {M}x{N}x{K}")
+    again = host(gpu.gemm(dev(a), dev(b), M=M, N=N, K=K, alpha=0.5, bias=dev(bias), act="sigmoid",
+                          residual=dev(res))).reshape(M, N)
+    np.testing.assert_array_equal(got, again)
+    plain = host(gpu.gemm(dev(a), dev(b), M=M, N=N, K=K)).reshape(M, N)
+    assert_dot_close(plain, O.sgemm(a, b), K, what=f"skinny bulk plain {M}x{N}x{K}")
+    gpu.device_status()

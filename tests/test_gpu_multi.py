@@ -81,8 +81,9 @@ def _partition_worker(rank, world, port, q):
     torch.cuda.set_device(rank)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     dev = torch.device("cuda", rank)
-    sd.init("nccl", timeout_s=120, device=dev)
     try:
+        sd.init("nccl", timeout_s=120, device=dev, init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                world_size=world)
         I = {k: torch.from_numpy(v).to(dev) for k, v in _partition_inputs().items()}
         res = {}
         c, _ = sd.dot(I["A"], I["B"], 1000, 640, 768)
@@ -106,7 +107,8 @@ def _partition_worker(rank, world, port, q):
     except Exception as e:  # noqa: BLE001
         q.put((rank, None, repr(e)))
     finally:
-        dist.destroy_process_group()
+        if dist.is_initialized():
+            dist.destroy_process_group()
 
 
 def test_two_gpu_partitioner(cuda):
@@ -127,7 +129,7 @@ def test_two_gpu_partitioner(cuda):
     procs = [ctx.Process(target=_partition_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    res = [q.get(timeout=600) for _ in procs]
+    res = [q.get(timeout=300) for _ in procs]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
