@@ -5,8 +5,17 @@ silarray's include/array.h declares seven members with C++23 explicit object
 parameters ("deducing this", include/array.h:353-379 and their definitions at
 953-969 and 1103-1142).  g++ 13 does not implement that feature.  This script
 rewrites exactly those members into const members that return T& / T* (the
-non-const instantiation the reference would pick for a mutable array) and
-changes nothing else.  The output goes to oracle/_ref/gen/array.h, is used only
+non-const instantiation the reference would pick for a mutable array).
+
+One defect fix as well: after evaluating a graph, array<T>::evaluate_node_
+and sil::eval (include/array.h:1973-1985, 2835-2888) clear the `visited` flag
+of every node in the topological order, but evaluating a node releases its
+inputs (array.h:2059-2060), so intermediate nodes nobody else holds are
+already freed: the clearing loop writes into freed memory (AddressSanitizer:
+heap-use-after-free at array.h:2881), which corrupted the heap in silarray's
+own bench_transformer.cpp on this backend.  The rewrite clears the flags
+right after the topological sort instead (they are only read by the sort),
+which changes nothing else.  The output goes to oracle/_ref/gen/array.h, is used only
 to compile the oracle library and the reference's own doctest suite, and is
 deleted by the Makefile after the build.
 
@@ -54,6 +63,32 @@ def patch(src: str) -> str:
         raise SystemExit(f"patch_ref: expected 7 definitions, rewrote {n}")
     if "this auto" in out:
         raise SystemExit("patch_ref: an explicit object parameter is left")
+
+    # The visited-flag reset, moved ahead of the evaluation loops.
+    a = ("  auto order = topo_sort_({node.get()});\n\n"
+         "  for (auto *cur : order) {\n"
+         "    if (cur->evaluated) continue;\n"
+         "    evaluate_single_node_(cur);\n"
+         "  }\n\n"
+         "  for (auto *cur : order) cur->visited = false;\n")
+    b = ("  auto order = topo_sort_({node.get()});\n"
+         "  for (auto *cur : order) cur->visited = false;\n\n"
+         "  for (auto *cur : order) {\n"
+         "    if (cur->evaluated) continue;\n"
+         "    evaluate_single_node_(cur);\n"
+         "  }\n")
+    if out.count(a) != 1:
+        raise SystemExit("patch_ref: evaluate_node_ loop not found")
+    out = out.replace(a, b)
+    a = ("  for (auto *cur : order) {\n"
+         "    if (cur->evaluated) continue;\n"
+         "    array<float>::evaluate_single_node_(cur);\n"
+         "  }\n")
+    c = "  for (auto *cur : order) cur->visited = false;\n\n  // Sync storage"
+    if out.count(a) != 1 or out.count(c) != 1:
+        raise SystemExit("patch_ref: sil::eval loops not found")
+    out = out.replace(c, "  // Sync storage")
+    out = out.replace(a, "  for (auto *cur : order) cur->visited = false;\n" + a)
     return out
 
 

@@ -606,7 +606,7 @@ size_t silcu_sgemm_workspace_bytes(const silcu_gemm_args *a) {
     case kPathTc: return tc_workspace_bytes(*a);
     case kPathSkinny: {
       if (a->M == 1) return gemv_part_bytes(gemv_plan(a->N, a->K), a->N);
-      if (skinny_bulk_eligible(*a)) return 0;
+      if (skinny_tma_eligible(*a)) return 0;
       return small_m_part_bytes(small_m_plan(a->M, a->N, a->K), a->M, a->N);
     }
     default: return 0;
@@ -642,7 +642,7 @@ silcu_status silcu_sgemm_ex(const silcu_gemm_args *ap, void *ws, size_t wsb, sil
     if (e != cudaSuccess) return fail(SILCU_CUDA_ERROR, "sgemm(gemv): %s", cudaGetErrorString(e));
     return check_launch("sgemm(gemv)", pl.groups > 1 ? 2 : 1);
   }
-  if (path == kPathSkinny && skinny_bulk_eligible(a)) return skinny_bulk_run(a, epi, s);
+  if (path == kPathSkinny && skinny_tma_eligible(a)) return skinny_tma_run(a, epi, s);
   if (path == kPathSkinny) {
     const SmallMPlan pl = small_m_plan(a.M, a.N, a.K);
     const size_t need = small_m_part_bytes(pl, a.M, a.N);

@@ -23,10 +23,10 @@ struct SkinnyEpi {
 };
 
 // Skinny GEMM (2 <= M <= 32, plain row-major operands whose rows are
-// 16-byte aligned): one wave of clusters streaming W by bulk copies
+// 16-byte aligned): one wave of clusters streaming W by TMA tile loads
 // (skinny.cu).  No workspace.
-bool skinny_bulk_eligible(const silcu_gemm_args &a);
-silcu_status skinny_bulk_run(const silcu_gemm_args &a, const SkinnyEpi &epi, cudaStream_t s);
+bool skinny_tma_eligible(const silcu_gemm_args &a);
+silcu_status skinny_tma_run(const silcu_gemm_args &a, const SkinnyEpi &epi, cudaStream_t s);
 
 // Workspace of the 3xTF32 path: the hi/lo split operands, K-major.
 size_t tc_workspace_bytes(const silcu_gemm_args &a);

@@ -6,11 +6,11 @@
 //   * the grid is (column blocks of 64) x (C slices of K); the C CTAs of a
 //     column block form one thread-block cluster, and C is chosen with the
 //     occupancy API so that every CTA of the grid is resident at once;
-//   * at start, warp 0 issues bulk copies (cp.async.bulk, no TMA descriptor)
-//     of the CTA's whole W slice (one 256-byte row per k) and X slice (one
-//     run per row of X) into shared memory: ~64-96 KB in flight per SM, the
-//     whole matrix requested in the first microseconds; the W rows land in
-//     chunks of 32 k, each with its own mbarrier, so the FMAs start on the
+//   * at start, one thread issues TMA tile loads of the CTA's whole W slice
+//     and X slice into shared memory (per chunk of 32 k: a 64-column x 32-row
+//     W box and a 32-k x R-row X box, zero-filled past K, N and M): ~100-200
+//     KB in flight per SM, the whole matrix requested in the first
+//     microseconds; each chunk has its own mbarrier, so the FMAs start on the
 //     first chunk while the rest streams in;
 //   * 256 threads: lane l owns columns 2l, 2l+1 of the block for all R rows
 //     (R = 16 or 32; 2R accumulators), warp w takes k = 4w..4w+3 of every
@@ -47,100 +47,76 @@ size_t smem_bytes(int kslice) {
   return kHead + (data > red ? data : red);
 }
 
+struct __align__(64) SkinnyMaps {
+  CUtensorMap w;  // W [K rows, N cols], boxes of 64 cols x 32 rows
+  CUtensorMap x;  // X [M rows, K cols], boxes of 32 k x R rows
+};
+
 template <int R>
 __global__ void __launch_bounds__(kThreads, 2)
-    skinny_gemm(const float *__restrict__ X, int64_t ldx, const float *__restrict__ W, int64_t ldw,
-                float *__restrict__ out, int64_t ldo, int M, int64_t N, int64_t K, int kslice, SkinnyEpi epi,
-                int *err) {
+    skinny_gemm(const __grid_constant__ SkinnyMaps maps, float *__restrict__ out, int64_t ldo, int M, int64_t N,
+                int64_t K, int kslice, SkinnyEpi epi, int *err) {
   namespace cg = cooperative_groups;
   extern __shared__ __align__(1024) uint8_t sm[];
-  uint64_t *bars = reinterpret_cast<uint64_t *>(sm);  // [0] = X, [1 + c] = W chunk c
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm);  // [c] = chunk c (W and X boxes)
   float *Ws = reinterpret_cast<float *>(sm + kHead);  // [kslice][64]
-  float *Xs = Ws + size_t(kslice) * kCols;           // [R][kslice]
+  float *Xs = Ws + size_t(kslice) * kCols;           // per chunk c: [R][32] at c * R * 32
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t col0 = int64_t(blockIdx.x) * kCols;
   const int64_t k0 = int64_t(blockIdx.y) * kslice;
   const int kn = int(k0 + kslice <= K ? kslice : (K > k0 ? K - k0 : 0));  // k rows of this slice
   const int nch = (kn + kChunk - 1) / kChunk;
-  const int wcols = int(N - col0 < kCols ? N - col0 : kCols);
-  const uint32_t wrow_bytes = uint32_t(wcols) * 4;
-  const int mrows = M < R ? M : R;
+  constexpr uint32_t kChunkBytes = uint32_t(kChunk) * (kCols + R) * 4;
 
   if (tid == 0) {
-    for (int c = 0; c <= nch; c++) tc::mbar_init(tc::smem_u32(bars + c), 1);
+    for (int c = 0; c < nch; c++) tc::mbar_init(tc::smem_u32(bars + c), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  if (warp == 0) {
-    if (lane == 0) {
-      if (kn > 0) tc::mbar_expect_tx(tc::smem_u32(bars), uint32_t(mrows) * uint32_t(kn) * 4);
-      for (int c = 0; c < nch; c++) {
-        const int rows = (c + 1) * kChunk <= kn ? kChunk : kn - c * kChunk;
-        tc::mbar_expect_tx(tc::smem_u32(bars + 1 + c), uint32_t(rows) * wrow_bytes);
-      }
-    }
-    __syncwarp();
-    // X rows first (every chunk needs them), then W rows in chunk order.
-    for (int m = lane; m < mrows && kn > 0; m += 32) {
-      const float *src = X + int64_t(m) * ldx + k0;
-      asm volatile(
-          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-              tc::smem_u32(Xs + size_t(m) * kslice)),
-          "l"(src), "r"(uint32_t(kn) * 4), "r"(tc::smem_u32(bars))
-          : "memory");
-    }
-    for (int k = lane; k < kn; k += 32) {
-      const float *src = W + (k0 + k) * ldw + col0;
-      asm volatile(
-          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-              tc::smem_u32(Ws + size_t(k) * kCols)),
-          "l"(src), "r"(wrow_bytes), "r"(tc::smem_u32(bars + 1 + k / kChunk))
-          : "memory");
+  if (tid == 0) {
+    // The whole slice at once: one W box and one X box per chunk (boxes past
+    // K or N read as zeros and still count their full size).
+    for (int c = 0; c < nch; c++) {
+      const uint32_t bar = tc::smem_u32(bars + c);
+      tc::mbar_expect_tx(bar, kChunkBytes);
+      const int kc = int(k0) + c * kChunk;
+      tc::tma_load_4d(tc::smem_u32(Ws + size_t(c) * kChunk * kCols), &maps.w, bar, int(col0), kc, 0, 0);
+      tc::tma_load_4d(tc::smem_u32(Xs + size_t(c) * R * kChunk), &maps.x, bar, kc, 0, 0, 0);
     }
   }
 
   float acc[R][2];
 #pragma unroll
   for (int r = 0; r < R; r++) acc[r][0] = acc[r][1] = 0.0f;
-  bool ok = kn == 0 || tc::mbar_wait(tc::smem_u32(bars), 0, err, 61);
-  for (int c = 0; c < nch && ok; c++) {
-    ok = tc::mbar_wait(tc::smem_u32(bars + 1 + c), 0, err, 62);
+  bool ok = true;
+  for (int c = 0; c < nch; c++) {
+    ok = tc::mbar_wait(tc::smem_u32(bars + c), 0, err, 62);
     if (!ok) break;
-    const int kb = c * kChunk + 4 * warp;  // this warp's 4 k of the chunk
-    if (kb >= kn) continue;
+    const int kk = 4 * warp;  // this warp's 4 k of the chunk (zeros past the slice end)
+    const float *wr = Ws + (size_t(c) * kChunk + kk) * kCols + 2 * lane;
     float w[4][2];
 #pragma unroll
     for (int u = 0; u < 4; u++) {
-      const float2 v = kb + u < kn ? *reinterpret_cast<const float2 *>(Ws + size_t(kb + u) * kCols + 2 * lane)
-                                   : make_float2(0.0f, 0.0f);
+      const float2 v = *reinterpret_cast<const float2 *>(wr + u * kCols);
       w[u][0] = v.x;
       w[u][1] = v.y;
     }
-    if (kb + 4 <= kn) {
+    const float *xr = Xs + size_t(c) * R * kChunk + kk;
 #pragma unroll
-      for (int r = 0; r < R; r++) {
-        const float4 x = *reinterpret_cast<const float4 *>(Xs + size_t(r) * kslice + kb);
-        acc[r][0] = fmaf(x.x, w[0][0], acc[r][0]);
-        acc[r][1] = fmaf(x.x, w[0][1], acc[r][1]);
-        acc[r][0] = fmaf(x.y, w[1][0], acc[r][0]);
-        acc[r][1] = fmaf(x.y, w[1][1], acc[r][1]);
-        acc[r][0] = fmaf(x.z, w[2][0], acc[r][0]);
-        acc[r][1] = fmaf(x.z, w[2][1], acc[r][1]);
-        acc[r][0] = fmaf(x.w, w[3][0], acc[r][0]);
-        acc[r][1] = fmaf(x.w, w[3][1], acc[r][1]);
-      }
-    } else {  // the slice's ragged end (K % 4 == 0, so kn % 4 == 0: not reached)
-      for (int u = 0; u < 4 && kb + u < kn; u++)
-#pragma unroll
-        for (int r = 0; r < R; r++) {
-          const float x = Xs[size_t(r) * kslice + kb + u];
-          acc[r][0] = fmaf(x, w[u][0], acc[r][0]);
-          acc[r][1] = fmaf(x, w[u][1], acc[r][1]);
-        }
+    for (int r = 0; r < R; r++) {
+      const float4 x = *reinterpret_cast<const float4 *>(xr + r * kChunk);
+      acc[r][0] = fmaf(x.x, w[0][0], acc[r][0]);
+      acc[r][1] = fmaf(x.x, w[0][1], acc[r][1]);
+      acc[r][0] = fmaf(x.y, w[1][0], acc[r][0]);
+      acc[r][1] = fmaf(x.y, w[1][1], acc[r][1]);
+      acc[r][0] = fmaf(x.z, w[2][0], acc[r][0]);
+      acc[r][1] = fmaf(x.z, w[2][1], acc[r][1]);
+      acc[r][0] = fmaf(x.w, w[3][0], acc[r][0]);
+      acc[r][1] = fmaf(x.w, w[3][1], acc[r][1]);
     }
   }
-  // Rows >= M hold values computed from unloaded shared memory; they are
-  // never stored.  The tree below sums warps in a fixed order.
+  // Rows >= M are zeros (the X boxes are zero-filled past M) and are never
+  // stored.  The tree below sums warps in a fixed order.
   __syncthreads();  // all FMAs done: the data region becomes the tree scratch
   float *tree = reinterpret_cast<float *>(sm + kHead);  // [4][R][64]
   float *part = tree + 4 * R * kCols;                   // [R][64] CTA partial
@@ -300,28 +276,34 @@ silcu_status run(const silcu_gemm_args &a, const SkinnyEpi &epi, cudaStream_t s)
   at[0].val.clusterDim.z = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, skinny_gemm<R>, a.A, int64_t(a.lda), a.B, int64_t(a.ldb), a.C,
-                                     int64_t(a.ldc), int(a.M), int64_t(a.N), int64_t(a.K), pl.kslice, epi, err);
+  SkinnyMaps maps;
+  const CUtensorMapSwizzle none = CU_TENSOR_MAP_SWIZZLE_NONE;
+  if (!tc::make_map4(&maps.w, a.B, a.N, a.K, a.ldb, 1, 0, 1, 0, kCols, kChunk, none) ||
+      !tc::make_map4(&maps.x, a.A, a.K, a.M, a.lda, 1, 0, 1, 0, kChunk, R, none))
+    return fail(SILCU_CUDA_ERROR, "sgemm(skinny): cuTensorMapEncodeTiled failed");
+  cudaError_t e = cudaLaunchKernelEx(&cfg, skinny_gemm<R>, maps, a.C, int64_t(a.ldc), int(a.M), int64_t(a.N),
+                                     int64_t(a.K), pl.kslice, epi, err);
   if (e != cudaSuccess) return fail(SILCU_CUDA_ERROR, "sgemm(skinny): %s", cudaGetErrorString(e));
   return check_launch("sgemm(skinny)");
 }
 
 }  // namespace
 
-bool skinny_bulk_eligible(const silcu_gemm_args &a) {
+bool skinny_tma_eligible(const silcu_gemm_args &a) {
   static const int off = [] {
-    const char *e = getenv("SILCU_SKINNY_BULK");
+    const char *e = getenv("SILCU_SKINNY_TMA");
     return e && atoi(e) == 0;
   }();
   if (off) return false;
-  // bulk copies need 16-byte aligned starts and sizes: N, K, lda, ldb
-  // multiples of 4 floats and 16-byte aligned bases.
+  // tensor maps need 16-byte aligned bases and row strides (lda, ldb
+  // multiples of 4 floats); the boxes' x coordinates (col0, k) are multiples
+  // of 32 floats.
   return a.M >= 2 && a.M <= 32 && !a.trans_a && !a.trans_b && a.batch == 1 && a.batch_inner <= 1 &&
-         a.N % 4 == 0 && a.K % 4 == 0 && a.lda % 4 == 0 && a.ldb % 4 == 0 && aligned16(a.A) && aligned16(a.B) &&
+         a.lda % 4 == 0 && a.ldb % 4 == 0 && aligned16(a.A) && aligned16(a.B) &&
          a.K >= 64 && a.K <= int64_t(16) * kChunk * kMaxChunks && (!a.residual || a.ldr >= a.N);
 }
 
-silcu_status skinny_bulk_run(const silcu_gemm_args &a, const SkinnyEpi &epi, cudaStream_t s) {
+silcu_status skinny_tma_run(const silcu_gemm_args &a, const SkinnyEpi &epi, cudaStream_t s) {
   return a.M <= 16 ? run<16>(a, epi, s) : run<32>(a, epi, s);
 }
 
