@@ -47,6 +47,14 @@ silcu_status silcu_synchronize(silcu_stream stream);
  * (SILCU_TIMEOUT when a wait gave up since the last call). */
 silcu_status silcu_device_status(silcu_stream stream);
 
+/* No counterpart in the reference: exercises the failure path of the bounded
+ * device waits.  One CTA waits on a barrier that nothing arrives at, through
+ * the same wait as the tensor-core kernels but with a limit of `limit_us`
+ * (1..1000000) microseconds; it then records code 77 in the device error
+ * word and returns, so the next silcu_device_status() on the stream reports
+ * SILCU_TIMEOUT (and clears it) while the context stays usable. */
+silcu_status silcu_check_bounded_wait(uint32_t limit_us, silcu_stream stream);
+
 /* ------------------------------------------------------------ elementwise
  * out[i] = a[i % len_a] (op) b[i % len_b] for i < n.  Replaces
  * gpu::add/sub/mul/div/pow<float|int> (include/gpu.h:289-312, kernels

@@ -74,6 +74,7 @@ _SIGS = {
     "silcu_kernel_launches": ([], C.c_ulonglong),
     "silcu_synchronize": ([vp], C.c_int),
     "silcu_device_status": ([vp], C.c_int),
+    "silcu_check_bounded_wait": ([u32, vp], C.c_int),
     "silcu_sigmoid_f32": ([vp, vp, sz, vp], C.c_int),
     "silcu_relu_f32": ([vp, vp, sz, vp], C.c_int),
     "silcu_sigmoid_backward_f32": ([vp, vp, vp, sz, vp], C.c_int),

@@ -4,6 +4,7 @@
 #include <string.h>
 
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace silcu {
 
@@ -54,9 +55,31 @@ silcu_status check_launch(const char *what, int launches) {
   return SILCU_OK;
 }
 
+// One CTA waits on an mbarrier that nothing arrives at, through the same
+// bounded wait as the tensor-core kernels but with the caller's limit.
+__global__ void bounded_wait_probe(int *err, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(tc::smem_u32(&bar), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  tc::mbar_wait_limit(tc::smem_u32(&bar), 0, err, 77, limit_ns);
+  __syncthreads();
+}
+
 }  // namespace silcu
 
 extern "C" {
+
+silcu_status silcu_check_bounded_wait(uint32_t limit_us, silcu_stream stream) {
+  if (limit_us == 0 || limit_us > 1000000u)
+    return silcu::fail(SILCU_INVALID_ARGUMENT, "check_bounded_wait: limit %u us outside 1..1000000", limit_us);
+  int *err = silcu::device_error_ptr();
+  if (!err) return silcu::fail(SILCU_CUDA_ERROR, "check_bounded_wait: no device error word");
+  silcu::bounded_wait_probe<<<1, 64, 0, silcu::as_stream(stream)>>>(err, 1000ull * limit_us);
+  return silcu::check_launch("check_bounded_wait");
+}
 
 const char *silcu_last_error(void) { return silcu::g_last_error; }
 

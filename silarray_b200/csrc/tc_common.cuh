@@ -46,8 +46,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait.  Returns false (and records `code`) when the phase does not
-// complete within WAIT_NS, or when another CTA already recorded an error.
-static __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *err, int code) {
+// complete within `limit_ns`, or when another CTA already recorded an error.
+static __device__ __noinline__ bool mbar_wait_limit(uint32_t bar, uint32_t parity, int *err, int code,
+                                                     unsigned long long limit_ns) {
   // try_wait suspends in hardware until the phase completes or a short time
   // limit passes, so the first polls cost nothing; the wall-clock limit (a
   // slow %globaltimer read) only starts after them.
@@ -58,12 +59,16 @@ static __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0) {
       if (*reinterpret_cast<volatile int *>(err) != 0) return false;
-      if (globaltimer() - t0 > WAIT_NS) {
+      if (globaltimer() - t0 > limit_ns) {
         atomicCAS(err, 0, code);
         return false;
       }
     }
   }
+}
+
+static __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *err, int code) {
+  return mbar_wait_limit(bar, parity, err, code, WAIT_NS);
 }
 
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0, int c1,
