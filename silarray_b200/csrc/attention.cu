@@ -7,22 +7,23 @@
 // kernel.  Both products are 3xTF32 (x = hi + lo, hi*hi + hi*lo + lo*hi) on
 // tcgen05.mma; each score is rounded once as fl(dot * scale) as the reference's
 // affine node does; the softmax is the streaming (online) form over key blocks
-// of 64, so the result equals the reference's up to fp32 rounding.
+// of 128, so the result equals the reference's up to fp32 rounding.
 //
-// One CTA = 128 query rows of one (batch, head); D = 64.
-//   warp 0     TMA: Q once (hi/lo), K blocks in a 2-stage ring, V^T blocks
-//   warp 1     TMEM alloc; one thread issues S_j = Q K_j^T into a double
-//              buffer, then O_j = P_{j-1} V_{j-1}, so S_{j+1} overlaps the
-//              softmax of block j
+// One CTA = 128 query rows of one (batch, head); D = 64; key blocks of 128.
+//   warp 0     TMA: Q once (hi/lo), then K and V blocks (one stage each,
+//              reloaded as soon as the MMA that read them completes)
+//   warp 1     TMEM alloc; one thread issues S_0, S_1, then per block j
+//              O_j = P_j V_j and S_{j+2} = Q K_{j+2}^T (S double-buffered, so
+//              the softmax of block j + 1 overlaps P.V of block j); the score
+//              MMAs have N = 128 (half as many as with 64-key blocks)
 //   warps 2-9  thread = query row (two warps per row quarter, each with half
-//              of the keys and of the output columns): scores from TMEM, running max / sum
-//              (exponentials on the hardware ex2 unit),
-//              P_j split into hi/lo into TMEM (the A operand of the P.V
-//              MMA), O accumulated in registers with
-//              round-to-nearest adds and rescaled as the max moves.
-// Shared memory: Q 64 KB + K 2 x 32 KB + V^T 2 x 32 KB = 192 KB.  P lives in
-// TMEM (the A operand of P.V is read from tensor memory), double-buffered
-// with O and the scores, so the softmax of block j + 1 overlaps P.V of block j.
+//              of the keys and of the output columns): scores from TMEM, running
+//              max / sum (exponentials on the hardware ex2 unit), P_j split into
+//              hi/lo into TMEM (hi over the scores it replaces, lo in its own
+//              columns: the A operand of the P.V MMA), O accumulated in registers
+//              with round-to-nearest adds and rescaled as the max moves.
+// Shared memory: Q 64 KB + K 64 KB + V 64 KB = 192 KB.  TMEM (512 columns):
+// S / P_hi 2 x 128, P_lo 128, O 2 x 64.
 // All waits are bounded (as in tc_gemm.cu); no TMA multicast, no clusters.
 #include <stdlib.h>
 #include <string.h>
@@ -35,27 +36,29 @@ namespace {
 using namespace tc;
 
 constexpr int QT = 128;  // query rows per CTA
-constexpr int KB = 64;   // keys per block
+constexpr int KB = 128;  // keys per block
 constexpr int HD = 64;   // head dimension
-constexpr int Q_ATOM = QT * 128;           // 16 KB: 128 rows x 32 fp32
-constexpr int K_ATOM = KB * 128;           // 8 KB
-constexpr int Q_BYTES = 2 * 2 * Q_ATOM;    // hi, lo x 2 atoms = 64 KB
-constexpr int K_STAGE = 2 * 2 * K_ATOM;    // 32 KB
-constexpr int V_BYTES = 2 * 2 * K_ATOM;    // V^T: 64 hd rows x 64 keys, hi/lo = 32 KB
-constexpr int OFF_Q = 0, OFF_K = Q_BYTES, OFF_V = OFF_K + 2 * K_STAGE;
-constexpr int DATA_BYTES = OFF_V + 2 * V_BYTES;  // 192 KB of 1024-aligned operand buffers
-// Ahead of them: 14 mbarriers + the TMEM slot (128 B) and the row max / sum
+constexpr int Q_ATOM = QT * 128;            // 16 KB: 128 rows x 32 fp32
+constexpr int K_ATOM = KB * 128;            // 16 KB: 128 key rows x 32 fp32 (also V rows)
+constexpr int VT_ATOM = HD * 128;           // 8 KB: V^T, 64 dim rows x 32 keys
+constexpr int Q_BYTES = 2 * 2 * Q_ATOM;     // hi, lo x 2 atoms = 64 KB
+constexpr int K_BYTES = 2 * 2 * K_ATOM;     // 64 KB
+constexpr int V_BYTES = 2 * HD * KB * 4;    // hi, lo of 64 x 128 = 64 KB
+constexpr int OFF_Q = 0, OFF_K = Q_BYTES, OFF_V = OFF_K + K_BYTES;
+constexpr int DATA_BYTES = OFF_V + V_BYTES;  // 192 KB of 1024-aligned operand buffers
+// Ahead of them: the mbarriers + the TMEM slot (256 B) and the row max / sum
 // exchange between the two softmax halves (2 x 2 x 128 floats).
 constexpr int HEAD_BYTES = 256 + 2 * 2 * QT * 4;
 constexpr int SMEM_BYTES = 232448;  // the per-CTA maximum; the data start is aligned up past HEAD_BYTES
 constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter: keys / output columns split in halves
 constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
-// TMEM columns: S_j in [64*(j&1), +64), O_j in [128 + 64*(j&1), +64),
-// P_j (A operand of P.V, hi then lo) in [256 + 128*(j&1), +128).
+// TMEM columns: S_j (then P_hi_j) in [128*(j&1), +128), P_lo in [256, 384),
+// O_j in [384 + 64*(j&1), +64).
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t COL_O = 128, COL_P = 256;
-constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(HD >> 3) << 17) |
-                           (uint32_t(QT >> 4) << 24);  // M=128, N=64 (both products)
+constexpr uint32_t COL_PLO = 256, COL_O = 384;
+constexpr uint32_t IDESC_BASE = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(QT >> 4) << 24);  // M = 128
+constexpr uint32_t IDESC_QK = IDESC_BASE | (uint32_t(KB >> 3) << 17);  // N = 128 keys
+constexpr uint32_t IDESC_PV = IDESC_BASE | (uint32_t(HD >> 3) << 17);  // N = 64 dims
 
 struct __align__(64) AttnParams {
   CUtensorMap q_hi, q_lo, k_hi, k_lo, v_hi, v_lo;  // 4-D {inner, rows, heads, batch}
@@ -72,7 +75,7 @@ struct __align__(64) AttnParams {
 // 128-byte swizzle with 32-byte atoms (descriptor layout 1), which the TMA
 // writes with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B: rows of 32 dims (128 B),
 // groups of 4 key rows 512 B apart (SBO), the second 32-dim box K_ATOM bytes
-// on (LBO = 8 KB).  One MMA (8 keys) spans two groups: 1024 B per k-step.
+// on (LBO = 16 KB).  One MMA (8 keys) spans two groups: 1024 B per k-step.
 __device__ __forceinline__ uint64_t make_desc_mn(uint32_t addr) {
   uint64_t d = 0;
   d |= uint64_t((addr & 0x3FFFFu) >> 4);
@@ -83,8 +86,8 @@ __device__ __forceinline__ uint64_t make_desc_mn(uint32_t addr) {
   return d;
 }
 
-enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kSEmpty = 11, kPFull = 13,
-           kPEmpty = 15, kOFull = 17, kOEmpty = 19, kNumBars = 21 };
+enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 2, kVFull = 3, kVEmpty = 4, kSFull = 5, kPFull = 7, kPEmpty = 8,
+           kOFull = 9, kOEmpty = 11, kNumBars = 13 };
 
 // D += A(TMEM, 128 x 8, K-major: lane = row, column = k) . B(shared memory).
 __device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
@@ -140,8 +143,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; i++) {
-      const bool epi = (i == kSEmpty || i == kSEmpty + 1 || i == kPFull || i == kPFull + 1 || i == kOEmpty ||
-                        i == kOEmpty + 1);
+      const bool epi = (i == kPFull || i == kOEmpty || i == kOEmpty + 1);
       mbar_init(bar(i), epi ? EPI_WARPS : 1);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -159,89 +161,66 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
 
   if (warp == 0) {
     if (lane == 0) {
-      bool ok = true;
       mbar_expect_tx(bar(kQFull), Q_BYTES);
       for (int a = 0; a < 2; a++) {
         tma_load_4d(base + OFF_Q + a * Q_ATOM, &p.q_hi, bar(kQFull), 32 * a, q0, h, b);
         tma_load_4d(base + OFF_Q + 2 * Q_ATOM + a * Q_ATOM, &p.q_lo, bar(kQFull), 32 * a, q0, h, b);
       }
       auto load_k = [&](int j) {
-        const int s = j & 1;
-        const uint32_t dst = base + OFF_K + s * K_STAGE;
-        mbar_expect_tx(bar(kKFull + s), K_STAGE);
+        mbar_expect_tx(bar(kKFull), K_BYTES);
         for (int a = 0; a < 2; a++) {
-          tma_load_4d(dst + a * K_ATOM, &p.k_hi, bar(kKFull + s), 32 * a, j * KB, h, b);
-          tma_load_4d(dst + 2 * K_ATOM + a * K_ATOM, &p.k_lo, bar(kKFull + s), 32 * a, j * KB, h, b);
+          tma_load_4d(base + OFF_K + a * K_ATOM, &p.k_hi, bar(kKFull), 32 * a, j * KB, h, b);
+          tma_load_4d(base + OFF_K + 2 * K_ATOM + a * K_ATOM, &p.k_lo, bar(kKFull), 32 * a, j * KB, h, b);
         }
       };
       auto load_v = [&](int j) {
-        const int st = j & 1;
-        const uint32_t dst = base + OFF_V + st * V_BYTES;
-        mbar_expect_tx(bar(kVFull + st), V_BYTES);
-        for (int a = 0; a < 2; a++) {
-          if (p.v_rows) {  // V rows: the boxes of K (32 dims x 64 keys), 32-byte-atom swizzle
-            tma_load_4d(dst + a * K_ATOM, &p.v_hi, bar(kVFull + st), 32 * a, j * KB, h, b);
-            tma_load_4d(dst + 2 * K_ATOM + a * K_ATOM, &p.v_lo, bar(kVFull + st), 32 * a, j * KB, h, b);
-          } else {
-            tma_load_4d(dst + a * K_ATOM, &p.v_hi, bar(kVFull + st), j * KB + 32 * a, 0, h, b);
-            tma_load_4d(dst + 2 * K_ATOM + a * K_ATOM, &p.v_lo, bar(kVFull + st), j * KB + 32 * a, 0, h, b);
+        mbar_expect_tx(bar(kVFull), V_BYTES);
+        if (p.v_rows) {  // V rows: the boxes of K (32 dims x 128 keys), 32-byte-atom swizzle
+          for (int a = 0; a < 2; a++) {
+            tma_load_4d(base + OFF_V + a * K_ATOM, &p.v_hi, bar(kVFull), 32 * a, j * KB, h, b);
+            tma_load_4d(base + OFF_V + 2 * K_ATOM + a * K_ATOM, &p.v_lo, bar(kVFull), 32 * a, j * KB, h, b);
+          }
+        } else {  // V^T: 4 boxes of 32 keys x 64 dims
+          for (int a = 0; a < KB / 32; a++) {
+            tma_load_4d(base + OFF_V + a * VT_ATOM, &p.v_hi, bar(kVFull), j * KB + 32 * a, 0, h, b);
+            tma_load_4d(base + OFF_V + V_BYTES / 2 + a * VT_ATOM, &p.v_lo, bar(kVFull), j * KB + 32 * a, 0, h, b);
           }
         }
       };
+      // K_j is reloaded once S_{j-1} has completed (KEmpty completion j), V_j
+      // once P.V_{j-1} has (VEmpty completion j); this order matches the order
+      // in which the MMA thread needs them.
       load_k(0);
       load_v(0);
+      bool ok = true;
       if (nb > 1) {
-        load_k(1);
-        load_v(1);
+        ok = mbar_wait(bar(kKEmpty), 0, p.err, 12);
+        if (ok) load_k(1);
       }
-      for (int j = 0; j + 2 < nb && ok; j++) {
-        if (!mbar_wait(bar(kKEmpty + (j & 1)), (j >> 1) & 1, p.err, 12)) { ok = false; break; }
-        load_k(j + 2);
-        if (!mbar_wait(bar(kVEmpty + (j & 1)), (j >> 1) & 1, p.err, 11)) { ok = false; break; }
-        load_v(j + 2);
+      for (int j = 1; j < nb && ok; j++) {
+        if (j + 1 < nb) {
+          if (!mbar_wait(bar(kKEmpty), j & 1, p.err, 12)) break;
+          load_k(j + 1);
+        }
+        if (!mbar_wait(bar(kVEmpty), (j - 1) & 1, p.err, 11)) break;
+        load_v(j);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // One thread issues 48 MMAs per key block, each small (N = 64), so the
-      // issue path is kept short: descriptors are built once per buffer and
-      // offset by constants (the start-address field is the low 14 bits of a
-      // descriptor, address / 16, so desc(a + o) = desc(a) + o / 16).
+      // Descriptors are built once per buffer and offset by constants (the
+      // start-address field is the low 14 bits of a descriptor, address / 16,
+      // so desc(a + o) = desc(a) + o / 16).
       const uint64_t dq = make_desc(base + OFF_Q);
-      const uint64_t dk0 = make_desc(base + OFF_K), dv0 = make_desc(base + OFF_V);
+      const uint64_t dk = make_desc(base + OFF_K), dv0 = make_desc(base + OFF_V);
       const uint64_t dvm = make_desc_mn(base + OFF_V);
+      const bool mn = p.v_rows != 0;
+      const uint32_t idesc_pv = mn ? (IDESC_PV | (1u << 16)) : IDESC_PV;  // B MN-major for V rows
       bool ok = mbar_wait(bar(kQFull), 0, p.err, 13);
-      auto pv = [&](int i) {
-        const int u = i & 1;
-        if (!mbar_wait(bar(kPFull + u), (i >> 1) & 1, p.err, 14)) return false;
-        if (!mbar_wait(bar(kVFull + u), (i >> 1) & 1, p.err, 15)) return false;
-        if (i >= 2 && !mbar_wait(bar(kOEmpty + u), ((i >> 1) & 1) ^ 1, p.err, 16)) return false;
+      auto qk = [&](int j) {  // S_j = Q K_j^T into buffer j & 1
+        if (!mbar_wait(bar(kKFull), j & 1, p.err, 17)) return false;
         tc_fence_after();
-        const uint32_t pcol = tmem + COL_P + 128 * u;
-        const bool mn = p.v_rows != 0;
-        const uint64_t dv = (mn ? dvm : dv0) + uint64_t((u * V_BYTES) >> 4);
-        const uint32_t idesc_pv = mn ? (IDESC | (1u << 16)) : IDESC;  // B MN-major for V rows
-#pragma unroll
-        for (int kk = 0; kk < KB / 8; kk++) {
-          // V^T: K-major, 8 keys = 32 bytes along a row; V rows: 8 keys = one 1024-byte row group.
-          const uint64_t vh = dv + uint64_t((mn ? kk * 1024 : (kk >> 2) * K_ATOM + (kk & 3) * 32) >> 4);
-          const uint64_t vl = vh + uint64_t((2 * K_ATOM) >> 4);
-          const uint32_t ph = pcol + 8 * kk, pl = pcol + 64 + 8 * kk;
-          mma_tf32_ts(tmem + COL_O + 64 * u, pl, vh, idesc_pv, kk == 0 ? 0u : 1u);
-          mma_tf32_ts(tmem + COL_O + 64 * u, ph, vl, idesc_pv, 1u);
-          mma_tf32_ts(tmem + COL_O + 64 * u, ph, vh, idesc_pv, 1u);
-        }
-        mma_commit(bar(kVEmpty + u));
-        mma_commit(bar(kPEmpty + u));
-        mma_commit(bar(kOFull + u));
-        return true;
-      };
-      for (int j = 0; j < nb && ok; j++) {
-        const int s = j & 1;
-        if (!mbar_wait(bar(kKFull + s), (j >> 1) & 1, p.err, 17)) { ok = false; break; }
-        if (j >= 2 && !mbar_wait(bar(kSEmpty + s), ((j >> 1) & 1) ^ 1, p.err, 18)) { ok = false; break; }
-        tc_fence_after();
-        const uint64_t dk = dk0 + uint64_t((s * K_STAGE) >> 4);
+        const uint32_t scol = tmem + 128 * (j & 1);
 #pragma unroll
         for (int kk = 0; kk < HD / 8; kk++) {
           const uint32_t off = (kk & 3) * 32;
@@ -249,15 +228,44 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
           const uint64_t ql = qh + uint64_t((2 * Q_ATOM) >> 4);
           const uint64_t kh = dk + uint64_t(((kk >> 2) * K_ATOM + off) >> 4);
           const uint64_t kl = kh + uint64_t((2 * K_ATOM) >> 4);
-          mma_tf32(tmem + 64 * s, ql, kh, IDESC, kk == 0 ? 0u : 1u);
-          mma_tf32(tmem + 64 * s, qh, kl, IDESC, 1u);
-          mma_tf32(tmem + 64 * s, qh, kh, IDESC, 1u);
+          mma_tf32(scol, ql, kh, IDESC_QK, kk == 0 ? 0u : 1u);
+          mma_tf32(scol, qh, kl, IDESC_QK, 1u);
+          mma_tf32(scol, qh, kh, IDESC_QK, 1u);
         }
-        mma_commit(bar(kKEmpty + s));
-        mma_commit(bar(kSFull + s));
-        if (j >= 1 && !pv(j - 1)) { ok = false; break; }
+        mma_commit(bar(kKEmpty));
+        mma_commit(bar(kSFull + (j & 1)));
+        return true;
+      };
+      auto pv = [&](int j) {  // O_j = P_j V_j into buffer j & 1
+        const int u = j & 1;
+        if (!mbar_wait(bar(kPFull), j & 1, p.err, 14)) return false;
+        if (!mbar_wait(bar(kVFull), j & 1, p.err, 15)) return false;
+        if (j >= 2 && !mbar_wait(bar(kOEmpty + u), ((j >> 1) & 1) ^ 1, p.err, 16)) return false;
+        tc_fence_after();
+        const uint32_t phi = tmem + 128 * u, plo = tmem + COL_PLO, ocol = tmem + COL_O + 64 * u;
+        const uint64_t dv = mn ? dvm : dv0;
+#pragma unroll
+        for (int kk = 0; kk < KB / 8; kk++) {
+          // V^T: K-major, 8 keys = 32 bytes along a row; V rows: 8 keys = one 1024-byte row group.
+          const uint64_t vh = dv + uint64_t((mn ? kk * 1024 : (kk >> 2) * VT_ATOM + (kk & 3) * 32) >> 4);
+          const uint64_t vl = vh + uint64_t((mn ? 2 * K_ATOM : V_BYTES / 2) >> 4);
+          mma_tf32_ts(ocol, plo + 8 * kk, vh, idesc_pv, kk == 0 ? 0u : 1u);
+          mma_tf32_ts(ocol, phi + 8 * kk, vl, idesc_pv, 1u);
+          mma_tf32_ts(ocol, phi + 8 * kk, vh, idesc_pv, 1u);
+        }
+        mma_commit(bar(kVEmpty));
+        mma_commit(bar(kPEmpty));
+        mma_commit(bar(kOFull + u));
+        return true;
+      };
+      if (ok) ok = qk(0);
+      if (ok && nb > 1) ok = qk(1);
+      for (int j = 0; j < nb && ok; j++) {
+        ok = pv(j);
+        // S_{j+2} reuses S_j's columns, which hold P_hi_j: issued after P.V_j,
+        // and MMAs of one thread run in issue order.
+        if (ok && j + 2 < nb) ok = qk(j + 2);
       }
-      if (ok && nb >= 1) pv(nb - 1);
     }
   } else {
     // Softmax warps: thread = query row r of the tile (TMEM lane r); the two
@@ -282,15 +290,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
       tc_fence_after();
       float sc[HK];
       {
-        uint32_t r0[32];
-        tmem_ld32_nowait(lane_base + 64 * s + HK * hh, r0);
+        uint32_t r0[32], r1[32];
+        tmem_ld32_nowait(lane_base + 128 * s + HK * hh, r0);
+        tmem_ld32_nowait(lane_base + 128 * s + HK * hh + 32, r1);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < HK; i++) sc[i] = __uint_as_float(r0[i]);
+        for (int i = 0; i < 32; i++) {
+          sc[i] = __uint_as_float(r0[i]);
+          sc[32 + i] = __uint_as_float(r1[i]);
+        }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kSEmpty + s));
       float mj = __int_as_float(0xff800000);
       const bool tail = (j + 1) * KB > p.Sk;
 #pragma unroll
@@ -313,32 +322,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
       }
       xsum[hh * QT + r] = ps;
       m = m_new;
-      // P_j (this half's 32 keys), split, into TMEM buffer j & 1 once P.V of
-      // block j - 2 has finished reading it.
-      if (j >= 2) {
-        bool w3 = mbar_wait(bar(kPEmpty + s), ((j >> 1) & 1) ^ 1, p.err, 22);
+      // P_j: hi over this half's scores (already read), lo into the P_lo
+      // columns once P.V_{j-1} has finished reading them.
+      if (j >= 1) {
+        bool w3 = mbar_wait(bar(kPEmpty), (j - 1) & 1, p.err, 22);
         if (!__all_sync(0xffffffffu, w3)) { ok = false; break; }
         tc_fence_after();
       }
-      {
+#pragma unroll
+      for (int c = 0; c < HK; c += 32) {
         uint32_t hv[32], lv[32];
         // P >= 0: round-to-nearest-away to tf32 is "add half a tf32 ulp,
         // clear the 13 low bits" (integer pipe, not the conversion unit).
 #pragma unroll
-        for (int i = 0; i < HK; i++) {
-          const uint32_t hb = (__float_as_uint(sc[i]) + 0x1000u) & 0xFFFFE000u;
+        for (int i = 0; i < 32; i++) {
+          const uint32_t hb = (__float_as_uint(sc[c + i]) + 0x1000u) & 0xFFFFE000u;
           hv[i] = hb;
-          lv[i] = __float_as_uint(__fsub_rn(sc[i], __uint_as_float(hb)));
+          lv[i] = __float_as_uint(__fsub_rn(sc[c + i], __uint_as_float(hb)));
         }
-        const uint32_t pcol = lane_base + COL_P + 128 * s + HK * hh;
-        tmem_st32(pcol, hv);
-        tmem_st32(pcol + 64, lv);
-        tmem_st_wait();
+        tmem_st32(lane_base + 128 * s + HK * hh + c, hv);
+        tmem_st32(lane_base + COL_PLO + HK * hh + c, lv);
       }
+      tmem_st_wait();
       tc_fence_before();
       asm volatile("bar.sync 1, 256;" ::: "memory");
       l = __fadd_rn(__fmul_rn(l, corr), __fadd_rn(xsum[r], xsum[QT + r]));
-      if (lane == 0) mbar_arrive(bar(kPFull + s));
+      if (lane == 0) mbar_arrive(bar(kPFull));
       if (j >= 1) {  // fold O_{j-1} (relative to the previous max) into o
         const int u = (j - 1) & 1;
         bool w2 = mbar_wait(bar(kOFull + u), ((j - 1) >> 1) & 1, p.err, 20);
