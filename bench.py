@@ -272,6 +272,17 @@ def run_suite(args, sink=None):
                       ldk=d, sk_b=S * d, sk_h=S * d, ldv=S, sv_b=d * S, sv_h=d * S, scale=0.125, O=Ob)
     emit("bmm attention 128x1024x1024x64 (fused)", timed(attention), flops=4.0 * BH * S * S * d,
          note="includes the splits of Q, K^T->K and V->V^T")
+    del Q, Kt, V, Ob
+    # beyond the metric's configurations: conv2d of the reference's bench/micro/bench_nn_ops.cpp
+    for (Nb, Ci, Co, Hh, Ww, Kk, desc) in ((1, 3, 32, 224, 224, 3, "ImageNet first layer"),
+                                           (16, 64, 128, 56, 56, 3, "ResNet mid layer"),
+                                           (16, 128, 256, 28, 28, 3, "ResNet deep layer")):
+        x = Nn(1, Nb, Hh, Ww, Ci)
+        wt = Nn(0.1, Co, Kk, Kk, Ci)
+        y = torch.empty(Nb * Hh * Ww * Co, device=dev)
+        emit(f"conv2d {desc} {Nb}x{Ci}x{Hh}x{Ww} k{Kk} -> {Co} (extra)", timed(lambda: gpu.conv2d(x, wt, y)),
+             flops=2.0 * Nb * Hh * Ww * Co * Kk * Kk * Ci, note="implicit GEMM, patch split included")
+        del x, wt, y
     return 0
 
 

@@ -529,11 +529,18 @@ class gpu {
     b200::queued();
   }
 
-  // conv2d and its transpose helper are not part of this backend.
-  template <class... A>
-  static void conv2d(A &&...) {
-    throw std::runtime_error("silarray b200: conv2d is not provided by this backend");
+  // include/gpu.h:815-833: NHWC input, OHWI weight, stride 1, padding K/2.
+  static void conv2d(const storage &input, const storage &weight, storage &output, uint32_t N, uint32_t H,
+                     uint32_t W, uint32_t C_in, uint32_t K, uint32_t C_out) {
+    b200::before_launch();
+    size_t need = silcu_conv2d_workspace_bytes(N, H, W, C_in, K, C_out);
+    void *ws = b200::workspace(need);
+    b200::check(silcu_conv2d_f32(b200::ptr<const float>(input), b200::ptr<const float>(weight),
+                                 b200::ptr<float>(output), N, H, W, C_in, K, C_out, ws, b200::workspace_cap(need),
+                                 b200::stream()));
+    b200::queued();
   }
+  // The transpose helper of the reference's conv2d path is not needed here.
   template <class... A>
   static void transpose(A &&...) {
     throw std::runtime_error("silarray b200: transpose kernel is not provided by this backend");

@@ -237,6 +237,16 @@ typedef struct silcu_gemm_args {
   float *C_hi, *C_lo;
 } silcu_gemm_args;
 
+/* gpu::conv2d (include/gpu.h:815-833; array::conv2d, include/array.h:1508-1519,
+ * 2259-2273): input NHWC [N, H, W, C_in], weight OHWI [C_out, K, K, C_in],
+ * stride 1, zero padding K / 2, output NHWC [N, H, W, C_out], no bias.  An
+ * implicit GEMM (M = N*H*W, N = C_out, K = K*K*C_in) on the 3xTF32 tensor-core
+ * path: one pass writes the split patch matrix into the workspace. */
+size_t silcu_conv2d_workspace_bytes(uint32_t N, uint32_t H, uint32_t W, uint32_t C_in, uint32_t K, uint32_t C_out);
+silcu_status silcu_conv2d_f32(const float *input, const float *weight, float *output, uint32_t N, uint32_t H,
+                              uint32_t W, uint32_t C_in, uint32_t K, uint32_t C_out, void *workspace,
+                              size_t workspace_bytes, silcu_stream stream);
+
 /* Exact tf32 split of a [rows, cols] fp32 matrix (row stride ld) into
  * contiguous hi/lo arrays, [rows, cols] or, when transpose, [cols, rows] --
  * how a constant weight W[K,N] is turned once into the K-major B_hi/B_lo

@@ -64,6 +64,7 @@ def _lib():
         "orc_sgemm_rows": [C.c_void_p, C.c_void_p, _f32p, _sz, _sz, _sz, _sz,
                            _sz, C.c_int, C.c_int, _sz, _sz],
         "orc_dot_i32": [_i32p, _i32p, _i32p, _sz, _sz, _sz],
+        "orc_conv2d_f32": [_f32p, _f32p, _f32p, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _sz],
     }
     for name, args in sig.items():
         getattr(lib, name).argtypes = args
@@ -201,6 +202,18 @@ def sgemm(a, b, ta=False, tb=False, rows=None):
     lib.orc_sgemm_rows(a.ctypes.data, b.ctypes.data, c, M, N, K, a.shape[1],
                        b.shape[1], int(ta), int(tb), r0, r1)
     return c
+
+
+def conv2d(x, w, rows=None):
+    """x [N,H,W,C] NHWC, w [C_out,K,K,C] OHWI -> [N*H*W, C_out] (stride 1,
+    padding K/2); ``rows`` = (m0, m1) restricts to a band of output pixels."""
+    x, w = _f(x), _f(w)
+    N, H, W, C = x.shape
+    C_out, K = w.shape[0], w.shape[1]
+    m0, m1 = rows or (0, N * H * W)
+    out = np.empty((m1 - m0, C_out), np.float32)
+    lib.orc_conv2d_f32(x.ravel(), w.ravel(), out, N, H, W, C, K, C_out, m0, m1)
+    return out
 
 
 def dot_i32(a, b):

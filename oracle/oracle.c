@@ -304,3 +304,35 @@ void orc_dot_i32(const int32_t *A, const int32_t *B, int32_t *C, size_t M,
         C[i * N + j] = (int32_t)((uint32_t)C[i * N + j] + a * (uint32_t)B[k * N + j]);
     }
 }
+
+/* conv2d (array::conv2d, include/array.h:1508-1519 and 2259-2273; gpu::conv2d,
+ * include/gpu.h:815-833 with the padding K/2 of gpu.h:713, 1202-1204): NHWC
+ * input [N,H,W,C], OHWI weight [C_out,K,K,C], stride 1, zero padding K/2,
+ * NHWC output [N,H,W,C_out].  The reference has no CPU path for conv2d (its
+ * benchmark notes "GPU only"), so this restates the GPU kernels' arithmetic:
+ * a dot product over (kh, kw, ci) per output, accumulated in fp64 and
+ * rounded once, like orc_sgemm_rows.  Rows [m0, m1) of the N*H*W output
+ * pixels only. */
+void orc_conv2d_f32(const float *in, const float *w, float *out, size_t N, size_t H, size_t W, size_t C,
+                    size_t K, size_t C_out, size_t m0, size_t m1) {
+  (void)N;
+  const long pad = (long)(K / 2);
+  for (size_t m = m0; m < m1; m++) {
+    const size_t n = m / (H * W), sp = m % (H * W), oh = sp / W, ow = sp % W;
+    for (size_t co = 0; co < C_out; co++) {
+      double s = 0.0;
+      for (size_t kh = 0; kh < K; kh++) {
+        const long ih = (long)oh + (long)kh - pad;
+        if (ih < 0 || ih >= (long)H) continue;
+        for (size_t kw = 0; kw < K; kw++) {
+          const long iw = (long)ow + (long)kw - pad;
+          if (iw < 0 || iw >= (long)W) continue;
+          const float *x = in + ((n * H + (size_t)ih) * W + (size_t)iw) * C;
+          const float *f = w + ((co * K + kh) * K + kw) * C;
+          for (size_t ci = 0; ci < C; ci++) s += (double)x[ci] * (double)f[ci];
+        }
+      }
+      out[(m - m0) * C_out + co] = (float)s;
+    }
+  }
+}

@@ -75,6 +75,8 @@ _SIGS = {
     "silcu_synchronize": ([vp], C.c_int),
     "silcu_device_status": ([vp], C.c_int),
     "silcu_check_bounded_wait": ([u32, vp], C.c_int),
+    "silcu_conv2d_workspace_bytes": ([u32, u32, u32, u32, u32, u32], sz),
+    "silcu_conv2d_f32": ([vp, vp, vp, u32, u32, u32, u32, u32, u32, vp, sz, vp], C.c_int),
     "silcu_sigmoid_f32": ([vp, vp, sz, vp], C.c_int),
     "silcu_relu_f32": ([vp, vp, sz, vp], C.c_int),
     "silcu_sigmoid_backward_f32": ([vp, vp, vp, sz, vp], C.c_int),

@@ -427,6 +427,21 @@ def sgemm_bias_sigmoid(A, B, C, bias, bias_len, M, N, K, lda, ldb):
     return gemm(A, B, C, M=M, N=N, K=K, lda=lda, ldb=ldb, bias=bias[:bias_len], act="sigmoid")
 
 
+def conv2d(input, weight, output=None, N=None, H=None, W=None, C_in=None, K=None, C_out=None):
+    """gpu::conv2d (include/gpu.h:815-833): NHWC input, OHWI weight, stride 1,
+    padding K/2; output [N*H*W, C_out]."""
+    _dev(input, _F32), _dev(weight, _F32)
+    if N is None:
+        N, H, W, C_in = input.shape
+        C_out, K = weight.shape[0], weight.shape[1]
+    if output is None:
+        output = torch.empty(N * H * W * C_out, dtype=_F32, device=input.device)
+    _dev(output, _F32)
+    wp, wn = _ws_args(lib().silcu_conv2d_workspace_bytes(N, H, W, C_in, K, C_out), input.device)
+    check(lib().silcu_conv2d_f32(_p(input), _p(weight), _p(output), N, H, W, C_in, K, C_out, wp, wn, _stream()))
+    return output
+
+
 def sgemv(x, W, y, N, K, bias=None):
     """gpu::sgemv (include/gpu.h:549-574): y[N] = x[K] . W[K,N] (+ bias)."""
     _dev(x, _F32), _dev(W, _F32), _dev(y, _F32)
