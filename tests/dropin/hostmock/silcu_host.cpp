@@ -234,6 +234,27 @@ silcu_status silcu_sgemm_ex(const silcu_gemm_args *ap, void *, size_t, silcu_str
   g_launches++;
   return SILCU_OK;
 }
+size_t silcu_conv2d_workspace_bytes(uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t) { return 0; }
+silcu_status silcu_conv2d_f32(const float *in, const float *w, float *out, uint32_t N, uint32_t H, uint32_t W,
+                              uint32_t C, uint32_t K, uint32_t Co, void *, size_t, silcu_stream) {
+  const long pad = long(K / 2);
+  for (size_t m = 0; m < size_t(N) * H * W; m++) {
+    const size_t n = m / (size_t(H) * W), sp = m % (size_t(H) * W), oh = sp / W, ow = sp % W;
+    for (size_t co = 0; co < Co; co++) {
+      double s = 0;
+      for (size_t kh = 0; kh < K; kh++)
+        for (size_t kw = 0; kw < K; kw++) {
+          const long ih = long(oh + kh) - pad, iw = long(ow + kw) - pad;
+          if (ih < 0 || ih >= long(H) || iw < 0 || iw >= long(W)) continue;
+          for (size_t ci = 0; ci < C; ci++)
+            s += double(in[((n * H + size_t(ih)) * W + size_t(iw)) * C + ci]) * double(w[((co * K + kh) * K + kw) * C + ci]);
+        }
+      out[m * Co + co] = float(s);
+    }
+  }
+  g_launches++;
+  return SILCU_OK;
+}
 size_t silcu_argmax_workspace_bytes(size_t, size_t) { return 0; }
 size_t silcu_sum_axis_workspace_bytes(size_t, size_t, size_t) { return 0; }
 size_t silcu_sgemm_workspace_bytes(const silcu_gemm_args *) { return 0; }
