@@ -330,6 +330,7 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
     float *st = ostage + (warp - 2) * 1024 * C::OUT_BUFS;
     uint32_t nstore = 0;
     const uint32_t rbar = rbar0 + 8 * (warp - 2);
+    const uint64_t out_policy = l2_policy_evict_first();  // outputs are not re-read by this kernel
     uint32_t rphase = 0;
     uint32_t cg = 0;
     bool ok = true;
@@ -350,16 +351,29 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
         if (!w) { ok = false; break; }
         tc_fence_after();
         const uint32_t src = tmem + (uint32_t(32 * q) << 16) + j * BN + h * EC;
+        if constexpr (EC >= 128) {
+          // 128 accumulators per thread: one 32-column load at a time keeps
+          // the drain within the register budget (no spills).
 #pragma unroll
-        for (int cc = 0; cc < EC / 32; cc += 2) {
-          uint32_t r0[32], r1[32];
-          tmem_ld32_nowait(src + uint32_t(32 * cc), r0);
-          tmem_ld32_nowait(src + uint32_t(32 * cc + 32), r1);
-          tmem_ld_wait();
+          for (int cc = 0; cc < EC / 32; cc++) {
+            uint32_t r0[32];
+            tmem_ld32_nowait(src + uint32_t(32 * cc), r0);
+            tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; i++) {
-            acc[32 * cc + i] = __fadd_rn(acc[32 * cc + i], __uint_as_float(r0[i]));
-            acc[32 * cc + 32 + i] = __fadd_rn(acc[32 * cc + 32 + i], __uint_as_float(r1[i]));
+            for (int i = 0; i < 32; i++) acc[32 * cc + i] = __fadd_rn(acc[32 * cc + i], __uint_as_float(r0[i]));
+          }
+        } else {
+#pragma unroll
+          for (int cc = 0; cc < EC / 32; cc += 2) {
+            uint32_t r0[32], r1[32];
+            tmem_ld32_nowait(src + uint32_t(32 * cc), r0);
+            tmem_ld32_nowait(src + uint32_t(32 * cc + 32), r1);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+              acc[32 * cc + i] = __fadd_rn(acc[32 * cc + i], __uint_as_float(r0[i]));
+              acc[32 * cc + 32 + i] = __fadd_rn(acc[32 * cc + 32 + i], __uint_as_float(r1[i]));
+            }
           }
         }
         tc_fence_before();
@@ -486,7 +500,7 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
             __syncwarp();
             if (lane == 0) {
               const CUtensorMap *m = o == 0 ? &p.c_map : (o == 1 ? &p.chi_map : &p.clo_map);
-              tma_store_4d(m, smem_u32(sb), col0, m0 + 32 * q, bi, bo);
+              tma_store_4d_hint(m, smem_u32(sb), col0, m0 + 32 * q, bi, bo, out_policy);
               bulk_commit();
             }
             nstore++;
