@@ -51,15 +51,16 @@ def parse():
 def ffn_up_case(dev, T=16384, d=768, f=3072):
     """Arguments of the forward's FFN-up GEMM (one tc_gemm_kernel launch):
     A = split layer_norm output [T, d], B = split K-major W1^T [f, d], bias +
-    relu epilogue, split output [T, f]."""
+    relu epilogue, split output [T, f], the block's accumulation chunk."""
     import torch
-    from silarray_b200 import gpu
+    from silarray_b200 import gpu, transformer
     g = torch.Generator(device=dev).manual_seed(0)
     A = torch.randn(T * d, device=dev, generator=g)
     W = torch.randn(d * f, device=dev, generator=g) * 0.02
     return dict(A=gpu.split(A, T, d), B=gpu.split(W, d, f, transpose=True), M=T, N=f, K=d, trans_b=True,
                 bias=torch.zeros(f, device=dev), act="relu", no_c=True,
-                C_split=(torch.empty(T * f, device=dev), torch.empty(T * f, device=dev)))
+                C_split=(torch.empty(T * f, device=dev), torch.empty(T * f, device=dev)),
+                acc_chunk_k=transformer.Block.ACC_CHUNK_K)
 
 
 def profile_case(args):

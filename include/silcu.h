@@ -235,6 +235,14 @@ typedef struct silcu_gemm_args {
    * the tensor-core path. */
   const float *A_hi, *A_lo, *B_hi, *B_lo;
   float *C_hi, *C_lo;
+  /* Tensor-core path: k values accumulated in one TMEM chunk before the
+   * epilogue adds the chunk into fp32 registers with round-to-nearest (the
+   * tensor core truncates as it accumulates).  0 = 128, the default that
+   * keeps general inputs (e.g. U[-1,1) at K = 8192) within the dot
+   * tolerance; a caller whose operand scales leave a wide margin (weights of
+   * ~0.02) may trade some of it for speed with longer chunks (a multiple of
+   * 16; the epilogue then stalls the MMAs less often). */
+  int32_t acc_chunk_k;
 } silcu_gemm_args;
 
 /* gpu::conv2d (include/gpu.h:815-833; array::conv2d, include/array.h:1508-1519,

@@ -50,7 +50,8 @@ class GemmArgs(C.Structure):
                 ("stride_c_inner", i64),
                 ("alpha", f32), ("bias", vp), ("bias_len", i64), ("act", i32),
                 ("residual", vp), ("ldr", i64), ("algo", i32),
-                ("A_hi", vp), ("A_lo", vp), ("B_hi", vp), ("B_lo", vp), ("C_hi", vp), ("C_lo", vp)]
+                ("A_hi", vp), ("A_lo", vp), ("B_hi", vp), ("B_lo", vp), ("C_hi", vp), ("C_lo", vp),
+                ("acc_chunk_k", i32)]
 
 
 class GemmPlan(C.Structure):

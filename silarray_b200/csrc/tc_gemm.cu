@@ -1015,7 +1015,7 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
   p.nbatch = int(nb);
   p.tma_c = tma_c ? 1 : 0;
   p.split_out = split_out ? 1 : 0;
-  p.chunk_kb = CHUNK_KB_DEFAULT;
+  p.chunk_kb = a.acc_chunk_k >= BK ? int(a.acc_chunk_k / BK) : CHUNK_KB_DEFAULT;
   if (const char *env = getenv("SILCU_TC_CHUNK_KB")) {  // tuning knob: K blocks per accumulation chunk
     const int v = atoi(env);
     if (v >= 1) p.chunk_kb = v;

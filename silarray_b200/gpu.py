@@ -349,13 +349,15 @@ ACT = {None: 0, "none": 0, "relu": 1, "sigmoid": 2}
 def gemm(A, B, C=None, *, M, N, K, lda=None, ldb=None, ldc=None, trans_a=False, trans_b=False,
          batch=1, stride_a=0, stride_b=0, stride_c=0, batch_inner=1, stride_a_inner=0,
          stride_b_inner=0, stride_c_inner=0, alpha=1.0, bias=None, act=None,
-         residual=None, ldr=None, algo="auto", C_split=None, no_c=False):
+         residual=None, ldr=None, algo="auto", C_split=None, no_c=False, acc_chunk_k=0):
     """C = act(alpha * op(A).op(B) + bias) + residual (silcu_sgemm_ex).
 
     A and B are CUDA float tensors, or (hi, lo) pairs holding the exact tf32
     split of the operand (what the tensor-core path consumes; written by
     producers with a split output).  C_split=(hi, lo) additionally writes the
-    split of the result; no_c=True writes only the split."""
+    split of the result; no_c=True writes only the split.  acc_chunk_k: k
+    values per TMEM accumulation chunk on the tensor-core path (0 = 128; see
+    silcu_gemm_args)."""
     def ops(X):
         if isinstance(X, (tuple, list)):
             _dev(X[0], _F32), _dev(X[1], _F32)
@@ -400,6 +402,7 @@ def gemm(A, B, C=None, *, M, N, K, lda=None, ldb=None, ldc=None, trans_a=False, 
         a.residual = residual.data_ptr()
         a.ldr = ldr if ldr is not None else N
     a.algo = ALGO[algo]
+    a.acc_chunk_k = int(acc_chunk_k)
     need = lib().silcu_sgemm_workspace_bytes(ct.byref(a))
     wp, wn = _ws_args(need, dev)
     check(lib().silcu_sgemm_ex(ct.byref(a), wp, wn, _stream()))
