@@ -244,7 +244,9 @@ def run_suite(args, sink=None):
                     ("argmax(axis=1)", 4.0 * R * C + 4.0 * R,
                      lambda i: (lambda X=rows_set(i): gpu.argmax_f32(X[0], X[2]))),
                     ("sum(axis=1)", 4.0 * R * C + 4.0 * R,
-                     lambda i: (lambda X=rows_set(i): gpu.sum_axis_f32(X[0], R, C, 1, X[1].view(-1)[:R])))):
+                     lambda i: (lambda X=rows_set(i): gpu.sum_axis_f32(X[0], R, C, 1, X[1].view(-1)[:R]))),
+                    ("sum(axis=1) in the reference's order (drop-in)", 4.0 * R * C + 4.0 * R,
+                     lambda i: (lambda X=rows_set(i): gpu.sum_axis_seq_f32(X[0], R, C, 1, X[1].view(-1)[:R])))):
                 emit(f"{name} 4096x{C}", timed_graph(mk, nb), nbytes=nb, timing="graph")
             sets.clear()
             continue
@@ -254,6 +256,8 @@ def run_suite(args, sink=None):
         emit(f"layer_norm 4096x{C}", timed(lambda: gpu.layer_norm(X, Y, gm, bt)), nbytes=8.0 * R * C + 8.0 * C)
         emit(f"argmax(axis=1) 4096x{C}", timed(lambda: gpu.argmax_f32(X)), nbytes=4.0 * R * C + 4.0 * R)
         emit(f"sum(axis=1) 4096x{C}", timed(lambda: gpu.sum_axis_f32(X, R, C, 1)), nbytes=4.0 * R * C + 4.0 * R)
+        emit(f"sum(axis=1) in the reference's order (drop-in) 4096x{C}", timed(lambda: gpu.sum_axis_seq_f32(X, R, C, 1)),
+             nbytes=4.0 * R * C + 4.0 * R)
         del X, Y
     Z = U(1 << 28)
     for name, fn in (("sum", gpu.sum_f32), ("min", gpu.min_f32), ("max", gpu.max_f32),

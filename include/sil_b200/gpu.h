@@ -420,6 +420,26 @@ class gpu {
     b200::queued();
   }
 
+  // Not part of the reference's interface: the drop-in build's evaluator calls
+  // it for sum(axis) where the reference loops on the host
+  // (include/array.h:2303-2317).  Up to 4096 terms per output the sums run in
+  // the loop's sequential order (the same bits); longer ones use the
+  // bandwidth-bound reduction (within 1e-5 of the sum of |x| of an fp64 sum),
+  // the rule silcu_sum_f32 follows for whole arrays.
+  static void sum_axis_f32(const storage &IN, storage &OUT, size_t outer, size_t len, size_t inner) {
+    b200::before_launch();
+    if (len <= 4096) {
+      b200::check(silcu_sum_axis_seq_f32(b200::ptr<const float>(IN), b200::ptr<float>(OUT), outer, len, inner,
+                                         b200::stream()));
+    } else {
+      size_t need = silcu_sum_axis_workspace_bytes(outer, len, inner);
+      void *ws = b200::workspace(need);
+      b200::check(silcu_sum_axis_f32(b200::ptr<const float>(IN), b200::ptr<float>(OUT), outer, len, inner, ws,
+                                     b200::workspace_cap(need), b200::stream()));
+    }
+    b200::queued();
+  }
+
   // include/gpu.h:473-501
   static void layer_norm(const storage &IN, storage &OUT, const storage &gamma, const storage &beta, uint32_t rows,
                          uint32_t cols, float eps) {

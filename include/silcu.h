@@ -187,6 +187,13 @@ size_t silcu_argmax_workspace_bytes(size_t rows, size_t cols);
 size_t silcu_sum_axis_workspace_bytes(size_t outer, size_t len, size_t inner);
 silcu_status silcu_sum_axis_f32(const float *in, float *out, size_t outer, size_t len, size_t inner,
                                 void *workspace, size_t workspace_bytes, silcu_stream stream);
+/* The same sum in the reference CPU loop's order (include/array.h:2303-2317,
+ * the branch silarray's evaluator runs on the host for every axis but 0 of a
+ * 2-D array): each output adds its inputs sequentially in fp32 in index order,
+ * so the result is bit-identical to the reference; one thread per output, no
+ * workspace.  The drop-in host layer routes sum(axis) here. */
+silcu_status silcu_sum_axis_seq_f32(const float *in, float *out, size_t outer, size_t len, size_t inner,
+                                    silcu_stream stream);
 
 /* ------------------------------------------------------------ GEMM family
  * C[M,N] = act(alpha * op(A) . op(B) + bias[col % bias_len]) (+ residual).

@@ -19,7 +19,13 @@ which changes nothing else.  The output goes to oracle/_ref/gen/array.h, is used
 to compile the oracle library and the reference's own doctest suite, and is
 deleted by the Makefile after the build.
 
-Usage: python oracle/patch_ref.py <reference include dir> <output file>
+With --dropin (the builds on the B200 backend headers only, never the CPU
+reference build): sum(axis) for every axis but 0 of a 2-D array runs the
+reference's own loop on the host even in GPU mode (include/array.h:2303-2317);
+the drop-in build routes dense inputs to gpu::sum_axis_f32, which adds in the
+same order on the GPU up to 4096 terms per output (bit-identical results).
+
+Usage: python oracle/patch_ref.py <reference include dir> <output file> [--dropin]
 """
 import re
 import sys
@@ -92,12 +98,45 @@ def patch(src: str) -> str:
     return out
 
 
+DROPIN_SUM_AXIS_FROM = """        } else {
+          input.enumerate_position_([&](const auto &pos) {
+            auto p = pos;
+            p.erase(p.begin() + axis);
+            tmp.at(p) += input.at(pos);
+          });
+        }
+        store_result(tmp);"""
+
+DROPIN_SUM_AXIS_TO = """        } else if (device_ == Device::MPS && input.buffer_element_count() == input.element_count()) {
+          size_t outer = 1, inner = 1;
+          for (size_t d = 0; d < axis; d++) outer *= in_shape[d];
+          for (size_t d = axis + 1; d < in_shape.size(); d++) inner *= in_shape[d];
+          gpu::sum_axis_f32(input.storage_, tmp.storage_, outer, in_shape[axis], inner);
+        } else {
+          input.enumerate_position_([&](const auto &pos) {
+            auto p = pos;
+            p.erase(p.begin() + axis);
+            tmp.at(p) += input.at(pos);
+          });
+        }
+        store_result(tmp);"""
+
+
+def patch_dropin(src: str) -> str:
+    if src.count(DROPIN_SUM_AXIS_FROM) != 1:
+        raise SystemExit("patch_ref: sum(axis) host loop not found")
+    return src.replace(DROPIN_SUM_AXIS_FROM, DROPIN_SUM_AXIS_TO)
+
+
 def main():
     src_dir, dst = sys.argv[1], sys.argv[2]
     with open(f"{src_dir}/array.h") as f:
         src = f.read()
+    out = patch(src)
+    if "--dropin" in sys.argv[3:]:
+        out = patch_dropin(out)
     with open(dst, "w") as f:
-        f.write(patch(src))
+        f.write(out)
 
 
 if __name__ == "__main__":

@@ -104,6 +104,7 @@ _SIGS = {
     "silcu_argmax_workspace_bytes": ([sz, sz], sz),
     "silcu_sum_axis_workspace_bytes": ([sz, sz, sz], sz),
     "silcu_sum_axis_f32": ([vp, vp, sz, sz, sz, vp, sz, vp], C.c_int),
+    "silcu_sum_axis_seq_f32": ([vp, vp, sz, sz, sz, vp], C.c_int),
     "silcu_sgemm_workspace_bytes": ([C.POINTER(GemmArgs)], sz),
     "silcu_sgemm_plan": ([C.POINTER(GemmArgs), C.POINTER(GemmPlan)], C.c_int),
     "silcu_sgemm_ex": ([C.POINTER(GemmArgs), vp, sz, vp], C.c_int),

@@ -1069,6 +1069,57 @@ size_t silcu_sum_axis_workspace_bytes(size_t outer, size_t len, size_t inner) {
   return sp > 1 ? size_t(sp) * outer * inner * sizeof(float) : 0;
 }
 
+// Sum over an axis in the reference CPU loop's order (include/array.h:
+// 2303-2317: every output accumulates its inputs sequentially in fp32, in
+// increasing index along the axis): one thread per output, so the result is
+// bit-identical to the reference.  Outputs along `inner` are consecutive
+// threads (coalesced loads); with inner == 1 a thread walks its contiguous
+// row with 16-byte loads, four sequential adds each.
+__global__ void __launch_bounds__(128) sum_axis_seq_kernel(const float *__restrict__ in, float *__restrict__ out,
+                                                          uint64_t outer, uint64_t len, uint64_t inner, int vec) {
+  const uint64_t total = outer * inner;
+  for (uint64_t g = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
+       g += uint64_t(gridDim.x) * blockDim.x) {
+    const uint64_t o = g / inner, i = g - o * inner;
+    const float *p = in + o * len * inner + i;
+    float s = 0.0f;
+    if (vec) {  // inner == 1, len % 4 == 0, 16-byte aligned rows
+      // 16 loads in flight per thread (one thread per row leaves few threads
+      // to hide memory latency with), then their 64 adds in order.
+      const float4 *p4 = reinterpret_cast<const float4 *>(p);
+      const uint64_t n4 = len / 4;
+      uint64_t k = 0;
+      for (; k + 16 <= n4; k += 16) {
+        float4 v[16];
+#pragma unroll
+        for (int u = 0; u < 16; u++) v[u] = __ldg(p4 + k + u);
+#pragma unroll
+        for (int u = 0; u < 16; u++) s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v[u].x), v[u].y), v[u].z), v[u].w);
+      }
+      for (; k < n4; k++) {
+        const float4 v = __ldg(p4 + k);
+        s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v.x), v.y), v.z), v.w);
+      }
+    } else {
+      for (uint64_t k = 0; k < len; k++) s = __fadd_rn(s, __ldg(p + k * inner));
+    }
+    out[g] = s;
+  }
+}
+
+silcu_status silcu_sum_axis_seq_f32(const float *in, float *out, size_t outer, size_t len, size_t inner,
+                                    silcu_stream stream) {
+  const size_t total = outer * inner;
+  if (total == 0) return SILCU_OK;
+  if (!in || !out) return fail(SILCU_INVALID_ARGUMENT, "sum_axis_seq: null pointer");
+  const int vec = inner == 1 && len % 4 == 0 && aligned16(in) ? 1 : 0;
+  uint64_t grid = (total + 127) / 128;
+  const uint64_t cap = uint64_t(sm_count()) * 16;
+  if (grid > cap) grid = cap;
+  sum_axis_seq_kernel<<<unsigned(grid), 128, 0, as_stream(stream)>>>(in, out, outer, len, inner, vec);
+  return check_launch("sum_axis_seq");
+}
+
 silcu_status silcu_sum_axis_f32(const float *in, float *out, size_t outer, size_t len, size_t inner, void *ws,
                                 size_t wsb, silcu_stream stream) {
   const size_t total = outer * inner;

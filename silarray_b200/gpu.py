@@ -335,6 +335,14 @@ def sum_axis_f32(IN, outer, length, inner, OUT=None):
     return OUT
 
 
+def sum_axis_seq_f32(IN, outer, length, inner, OUT=None):
+    """Sum over an axis in the reference CPU loop's order (bit-identical)."""
+    _dev(IN, _F32)
+    OUT = torch.empty(outer * inner, dtype=_F32, device=IN.device) if OUT is None else _dev(OUT, _F32)
+    check(lib().silcu_sum_axis_seq_f32(_p(IN), _p(OUT), outer, length, inner, _stream()))
+    return OUT
+
+
 def sum_axis0_f32(IN, OUT=None, rows=None, cols=None):
     """gpu::sum_axis0_f32 (include/gpu.h:385-406): column sums of [rows, cols]."""
     rows, cols = (IN.shape[0], IN.shape[1]) if rows is None else (rows, cols)

@@ -102,6 +102,35 @@ int main() {
     expect(rel < 1e-4, "chain feeding a whole-array sum");
   }
 
+  // sum(axis) for axes the reference sums on the host: on the GPU in the same
+  // sequential order, so bit-identical to the CPU path.
+  {
+    auto t3 = random({7, 300, 33});
+    for (size_t axis : {size_t(1), size_t(2)}) {
+      use_cuda();
+      auto n0 = silcu_kernel_launches();
+      auto g = t3.sum(axis);
+      eval(g);
+      auto launches = silcu_kernel_launches() - n0;
+      use_cpu();
+      auto c = t3.sum(axis);
+      eval(c);
+      use_cuda();
+      char msg[128];
+      std::snprintf(msg, sizeof(msg), "sum(axis=%zu) of [7,300,33] on the GPU, bit-identical to the CPU path", axis);
+      expect(launches == 1 && same_bits(g, c), msg);
+    }
+    auto m2 = random({4096, 1024});
+    use_cuda();
+    auto g = m2.sum(1);
+    eval(g);
+    use_cpu();
+    auto c = m2.sum(1);
+    eval(c);
+    use_cuda();
+    expect(same_bits(g, c), "sum(axis=1) of [4096,1024], bit-identical to the CPU path");
+  }
+
   std::printf("%s (%d failure(s))\n", failures ? "FAILED" : "PASSED", failures);
   return failures ? 1 : 0;
 }

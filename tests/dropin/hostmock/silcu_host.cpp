@@ -255,6 +255,16 @@ silcu_status silcu_conv2d_f32(const float *in, const float *w, float *out, uint3
   g_launches++;
   return SILCU_OK;
 }
+silcu_status silcu_sum_axis_seq_f32(const float *in, float *out, size_t outer, size_t len, size_t inner, silcu_stream) {
+  for (size_t o = 0; o < outer; o++)
+    for (size_t i = 0; i < inner; i++) {
+      float s = 0.0f;
+      for (size_t l = 0; l < len; l++) s += in[(o * len + l) * inner + i];
+      out[o * inner + i] = s;
+    }
+  g_launches++;
+  return SILCU_OK;
+}
 size_t silcu_argmax_workspace_bytes(size_t, size_t) { return 0; }
 size_t silcu_sum_axis_workspace_bytes(size_t, size_t, size_t) { return 0; }
 size_t silcu_sgemm_workspace_bytes(const silcu_gemm_args *) { return 0; }

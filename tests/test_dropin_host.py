@@ -22,7 +22,7 @@ def test_chain_fusion_host_logic(tmp_path):
     gen = tmp_path / "gen"
     gen.mkdir()
     subprocess.run(["python", os.path.join(ROOT, "oracle", "patch_ref.py"), os.path.join(REF, "include"),
-                    str(gen / "array.h")], check=True)
+                    str(gen / "array.h"), "--dropin"], check=True)
     blasdir = os.path.join(sysconfig.get_paths()["purelib"], "opencv_python_headless.libs")
     blas = [os.path.join(blasdir, f) for f in os.listdir(blasdir) if f.startswith("libopenblasp-")]
     exe = tmp_path / "chain_fusion_host"

@@ -177,3 +177,16 @@ def test_small_sum_is_sequential_fp32(cuda, n):
     """Up to 4096 elements the sum is the reference's sequential fp32 sum, bit for bit."""
     x = np.random.default_rng(n).uniform(-1, 1, n).astype(np.float32)
     assert host(gpu.sum_f32(dev(x))) == O.sum_all(x)
+
+
+@pytest.mark.parametrize("shape,axis", [((7, 300, 33), 0), ((7, 300, 33), 1), ((7, 300, 33), 2),
+                                        ((4096, 1024), 1), ((3, 5), 1), ((2, 1001), 1)])
+def test_sum_axis_sequential_bit_exact(cuda, shape, axis):
+    """silcu_sum_axis_seq_f32 adds in the reference CPU loop's order
+    (include/array.h:2303-2317): bit-identical to the oracle's restatement."""
+    rng = np.random.default_rng(sum(shape) + axis)
+    x = rng.normal(0, 1, shape).astype(np.float32)
+    outer = int(np.prod(shape[:axis], dtype=np.int64))
+    inner = int(np.prod(shape[axis + 1:], dtype=np.int64))
+    got = host(gpu.sum_axis_seq_f32(dev(x.ravel()), outer, shape[axis], inner))
+    np.testing.assert_array_equal(got, O.sum_axis(x, axis).ravel())
