@@ -197,8 +197,10 @@ class Block:
         """Forwards of consecutive batches from host to host, overlapped
         across batches: while batch k computes, batch k + 1 is copied in and
         batch k - 1 is copied out (three streams, two device buffers each for
-        input and output).  x_hosts / out_hosts are sequences of pinned host
-        buffers of cfg.tokens x d_model floats (an output buffer may be listed
+        input and output); the first and the last batch run as two
+        half-batches, so their unoverlapped copies shrink by half.  x_hosts /
+        out_hosts are sequences of pinned host buffers of cfg.tokens x d_model
+        floats (an output buffer may be listed
         again two or more batches later: the copies into it stay in order).
         Ordered on the current stream: when it completes, every out_hosts[k]
         holds the forward of x_hosts[k]."""
@@ -220,24 +222,39 @@ class Block:
         self._s_out2.wait_stream(comp)
         computed = [None, None]  # per device buffer: the compute that last read din / wrote dout
         copied_out = [None, None]  # per device buffer: the copy that last read dout
-        for k in range(len(x_hosts)):
+        nbat = len(x_hosts)
+        S, d, B = cfg.seq, cfg.d_model, cfg.batch
+        for k in range(nbat):
             i = k & 1
+            # The first and the last batch run as two half-batches, so that
+            # the copy that nothing else can overlap (the first in, the last
+            # out) overlaps the other half's compute.
+            halves = [(0, B // 2), (B // 2, B - B // 2)] if (k == 0 or k == nbat - 1) and B >= 2 else [(0, B)]
             with torch.cuda.stream(self._s_in2):
                 if computed[i] is not None:
                     self._s_in2.wait_event(computed[i])  # din[i] free once batch k - 2 computed
-                din[i].copy_(x_hosts[k].reshape(-1), non_blocking=True)
-                ready = torch.cuda.Event()
-                ready.record(self._s_in2)
-            comp.wait_event(ready)
+                ready = []
+                for b0, nb in halves:
+                    r0, r1 = b0 * S * d, (b0 + nb) * S * d
+                    din[i][r0:r1].copy_(x_hosts[k].reshape(-1)[r0:r1], non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(self._s_in2)
+                    ready.append(ev)
             if copied_out[i] is not None:
                 comp.wait_event(copied_out[i])  # dout[i] read out for batch k - 2
-            self._run(din[i], dout[i], 0, cfg.batch)
-            done = torch.cuda.Event()
-            done.record(comp)
-            computed[i] = done
+            done = []
+            for (b0, nb), ev in zip(halves, ready):
+                comp.wait_event(ev)
+                self._run(din[i], dout[i], b0, nb)
+                dn = torch.cuda.Event()
+                dn.record(comp)
+                done.append(dn)
+            computed[i] = done[-1]
             with torch.cuda.stream(self._s_out2):
-                self._s_out2.wait_event(done)
-                out_hosts[k].reshape(-1).copy_(dout[i], non_blocking=True)
+                for (b0, nb), dn in zip(halves, done):
+                    r0, r1 = b0 * S * d, (b0 + nb) * S * d
+                    self._s_out2.wait_event(dn)
+                    out_hosts[k].reshape(-1)[r0:r1].copy_(dout[i][r0:r1], non_blocking=True)
                 c = torch.cuda.Event()
                 c.record(self._s_out2)
             copied_out[i] = c

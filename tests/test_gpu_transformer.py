@@ -49,8 +49,12 @@ def test_forward_host_chunks(cuda, chunks):
 def test_forward_host_stream(cuda):
     """Consecutive batches host to host with the copies of neighbouring
     batches overlapping the compute: each output equals the device forward of
-    its input bit for bit, in one call over five batches and in five calls of
-    one batch whose outputs alternate between two host buffers."""
+    its input -- bit for bit for the middle batches, and within the block's
+    tolerance for the first and the last, which run as two half-batches (their
+    GEMMs may take other split-K plans, so other rounding) -- in one call over
+    five batches and in five calls of one batch whose outputs alternate
+    between two host buffers."""
+    from oracle import transformer_ref as TR
     cfg = transformer.Config(batch=4, seq=256, d_model=256, heads=4, d_ff=1024)
     p = transformer.init_params(cfg, seed=7)
     blk = transformer.Block(cfg, p, device="cuda")
@@ -58,18 +62,25 @@ def test_forward_host_stream(cuda):
     want = [blk.forward(torch.from_numpy(x).cuda()).cpu().numpy() for x in xs]
     xh = [torch.from_numpy(x).pin_memory() for x in xs]
     oh = [torch.empty(cfg.tokens * cfg.d_model, dtype=torch.float32).pin_memory() for _ in range(5)]
+
+    def same(got, k, exact):
+        got = got.reshape(want[k].shape)
+        if exact:
+            np.testing.assert_array_equal(got, want[k])
+        else:
+            TR.check_parity(got, want[k].astype(np.float64), cfg)
     blk.forward_host_stream(xh, oh)
     torch.cuda.synchronize()
     for k in range(5):
-        np.testing.assert_array_equal(oh[k].numpy().reshape(want[k].shape), want[k])
+        same(oh[k].numpy(), k, 0 < k < 4)
     ring = [torch.empty(cfg.tokens * cfg.d_model, dtype=torch.float32).pin_memory() for _ in range(2)]
     got = []
-    for k in range(5):  # one batch per call, outputs read back between calls
+    for k in range(5):  # one batch per call (each both first and last), outputs read back between calls
         blk.forward_host_stream([xh[k]], [ring[k % 2]])
         torch.cuda.synchronize()
         got.append(ring[k % 2].numpy().copy())
     for k in range(5):
-        np.testing.assert_array_equal(got[k].reshape(want[k].shape), want[k])
+        same(got[k], k, False)
     gpu.device_status()
 
 
