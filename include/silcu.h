@@ -305,6 +305,16 @@ typedef struct silcu_attention_args {
 } silcu_attention_args;
 silcu_status silcu_attention_f32(const silcu_attention_args *args_host, silcu_stream stream);
 
+/* The same with a workspace: when the (batch, head, query tile) units leave
+ * the last wave of SMs mostly idle and the key axis is long enough, each
+ * unit's key blocks are split into up to 4 contiguous ranges computed by
+ * separate CTAs and combined (m, l rescaling) in a second pass.  The
+ * workspace size depends on the shape only (0 when no split is taken);
+ * with a smaller workspace the call runs unsplit. */
+size_t silcu_attention_workspace_bytes(const silcu_attention_args *args_host);
+silcu_status silcu_attention_ex(const silcu_attention_args *args_host, void *workspace, size_t workspace_bytes,
+                                silcu_stream stream);
+
 /* The general GEMM of the reference's dot / linear / linear_sigmoid /
  * batched_dot nodes.  The workspace (size from silcu_sgemm_workspace_bytes,
  * 0 when none is needed) holds the tf32 splits of operands given plain and,

@@ -101,6 +101,8 @@ _SIGS = {
     "silcu_split_f32": ([vp, sz, sz, sz, C.c_int, vp, vp, vp], C.c_int),
     "silcu_transpose_split_f32": ([vp, vp, sz, sz, sz, sz, sz, sz, sz, vp, vp, vp], C.c_int),
     "silcu_attention_f32": ([C.POINTER(AttnArgs), vp], C.c_int),
+    "silcu_attention_workspace_bytes": ([C.POINTER(AttnArgs)], C.c_size_t),
+    "silcu_attention_ex": ([C.POINTER(AttnArgs), vp, C.c_size_t, vp], C.c_int),
     "silcu_argmax_workspace_bytes": ([sz, sz], sz),
     "silcu_sum_axis_workspace_bytes": ([sz, sz, sz], sz),
     "silcu_sum_axis_f32": ([vp, vp, sz, sz, sz, vp, sz, vp], C.c_int),

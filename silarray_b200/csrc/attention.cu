@@ -9,13 +9,17 @@
 // affine node does; the softmax is the streaming (online) form over key blocks
 // of 128, so the result equals the reference's up to fp32 rounding.
 //
-// One CTA = 128 query rows of one (batch, head); D = 64; key blocks of 128.
-//   warp 0     TMA: Q once (hi/lo), then K and V blocks (one stage each,
+// Persistent: one CTA per SM takes work items (128 query rows of one
+// (batch, head), against all key blocks of 128 or, with a split key axis,
+// a range of them) round-robin, and streams the key blocks of all its items
+// through one pipeline, so an item's first loads and score products overlap
+// the previous item's last blocks.  D = 64.
+//   warp 0     TMA: per item Q (hi/lo), then K and V blocks (one stage each,
 //              reloaded as soon as the MMA that read them completes)
-//   warp 1     TMEM alloc; one thread issues S_0, S_1, then per block j
-//              O_j = P_j V_j and S_{j+2} = Q K_{j+2}^T (S double-buffered, so
-//              the softmax of block j + 1 overlaps P.V of block j); the score
-//              MMAs have N = 128 (half as many as with 64-key blocks)
+//   warp 1     TMEM alloc; one thread issues S_0, S_1, then per block t
+//              O_t = P_t V_t and S_{t+2} = Q K_{t+2}^T (S double-buffered, so
+//              the softmax of block t + 1 overlaps P.V of block t); the score
+//              MMAs have N = 128
 //   warps 2-9  thread = query row (two warps per row quarter, each with half
 //              of the keys and of the output columns): scores from TMEM, running
 //              max / sum (exponentials on the hardware ex2 unit), P_j split into
@@ -68,6 +72,50 @@ struct __align__(64) AttnParams {
   int v_rows;  // V given as [Sk, D] rows (B operand of P.V read MN-major), else V^T [D, Sk]
   float scale;
   int *err;
+  // Split KV: the key blocks of each (batch, head, query tile) in kv_splits
+  // contiguous ranges, one CTA each; with kv_splits > 1 a CTA writes its
+  // unnormalised O rows, row max m and row sum l to part_o / part_ml and
+  // attn_combine forms the output.
+  int kv_splits, units, items;  // items = units x kv_splits
+  float *part_o, *part_ml;
+};
+
+// A work item: the query tile q0 of head h of batch b against the key
+// blocks [kb0, kb0 + nb) (range sp of the unit's kv_splits).
+struct Item {
+  int q0, h, b, kb0, nb, unit, sp;
+};
+
+__device__ __forceinline__ Item item_of(const AttnParams &p, int w) {
+  Item it;
+  it.unit = w / p.kv_splits;
+  it.sp = w - it.unit * p.kv_splits;
+  const int qt = it.unit % p.tiles_q, bh = it.unit / p.tiles_q;
+  it.h = bh % p.heads;
+  it.b = bh / p.heads;
+  it.q0 = qt * QT;
+  const int nbt = (p.Sk + KB - 1) / KB;
+  it.kb0 = it.sp * nbt / p.kv_splits;
+  it.nb = (it.sp + 1) * nbt / p.kv_splits - it.kb0;
+  return it;
+}
+
+// Position in this CTA's stream of key blocks: item i (= w), block j of it.
+struct Cursor {
+  const AttnParams &p;
+  int i, w, j;
+  Item it;
+  __device__ explicit Cursor(const AttnParams &pp) : p(pp), i(0), w(blockIdx.x), j(0) {
+    if (w < p.items) it = item_of(p, w);
+  }
+  __device__ void next() {
+    if (++j == it.nb) {
+      j = 0;
+      i++;
+      w += gridDim.x;
+      if (w < p.items) it = item_of(p, w);
+    }
+  }
 };
 
 // Descriptor of V [keys, dims] rows as the MN-major B operand of P.V (N =
@@ -136,10 +184,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
   auto bar = [&](int i) { return smem_u32(bars + i); };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = blockIdx.x % p.tiles_q, bh = blockIdx.x / p.tiles_q;
-  const int h = bh % p.heads, b = bh / p.heads;
-  const int q0 = qt * QT;
-  const int nb = (p.Sk + KB - 1) / KB;
+  // This CTA's work items w = blockIdx.x + i * gridDim.x (w < p.items), each
+  // a (batch, head, query tile, key range); their key blocks form one stream
+  // t = 0 .. T-1 through the pipeline, so the next item's Q, K, V loads and
+  // first score products overlap the current item's last blocks.
+  int T = 0;
+  for (int w = blockIdx.x; w < p.items; w += gridDim.x) T += item_of(p, w).nb;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; i++) {
@@ -160,54 +210,66 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
   const uint32_t base = smem_u32(smem);
 
   if (warp == 0) {
-    if (lane == 0) {
-      mbar_expect_tx(bar(kQFull), Q_BYTES);
-      for (int a = 0; a < 2; a++) {
-        tma_load_4d(base + OFF_Q + a * Q_ATOM, &p.q_hi, bar(kQFull), 32 * a, q0, h, b);
-        tma_load_4d(base + OFF_Q + 2 * Q_ATOM + a * Q_ATOM, &p.q_lo, bar(kQFull), 32 * a, q0, h, b);
-      }
-      auto load_k = [&](int j) {
+    if (lane == 0 && T > 0) {
+      // K_{t+1} is loaded once S_t has completed (KEmpty completion t), V_t
+      // once P.V_{t-1} has (VEmpty completion t - 1): the order in which the
+      // MMA thread needs them.  An item's Q goes with its first K: S_t, the
+      // last score product of the previous item, has then finished reading
+      // the old Q.
+      Cursor ck(p), cv(p);
+      auto load_k = [&](const Cursor &c) {
+        if (c.j == 0) {
+          mbar_expect_tx(bar(kQFull), Q_BYTES);
+          for (int a = 0; a < 2; a++) {
+            tma_load_4d(base + OFF_Q + a * Q_ATOM, &p.q_hi, bar(kQFull), 32 * a, c.it.q0, c.it.h, c.it.b);
+            tma_load_4d(base + OFF_Q + 2 * Q_ATOM + a * Q_ATOM, &p.q_lo, bar(kQFull), 32 * a, c.it.q0, c.it.h,
+                        c.it.b);
+          }
+        }
+        const int key = (c.it.kb0 + c.j) * KB;
         mbar_expect_tx(bar(kKFull), K_BYTES);
         for (int a = 0; a < 2; a++) {
-          tma_load_4d(base + OFF_K + a * K_ATOM, &p.k_hi, bar(kKFull), 32 * a, j * KB, h, b);
-          tma_load_4d(base + OFF_K + 2 * K_ATOM + a * K_ATOM, &p.k_lo, bar(kKFull), 32 * a, j * KB, h, b);
+          tma_load_4d(base + OFF_K + a * K_ATOM, &p.k_hi, bar(kKFull), 32 * a, key, c.it.h, c.it.b);
+          tma_load_4d(base + OFF_K + 2 * K_ATOM + a * K_ATOM, &p.k_lo, bar(kKFull), 32 * a, key, c.it.h, c.it.b);
         }
       };
-      auto load_v = [&](int j) {
+      auto load_v = [&](const Cursor &c) {
+        const int key = (c.it.kb0 + c.j) * KB;
         mbar_expect_tx(bar(kVFull), V_BYTES);
         if (p.v_rows) {  // V rows: the boxes of K (32 dims x 128 keys), 32-byte-atom swizzle
           for (int a = 0; a < 2; a++) {
-            tma_load_4d(base + OFF_V + a * K_ATOM, &p.v_hi, bar(kVFull), 32 * a, j * KB, h, b);
-            tma_load_4d(base + OFF_V + 2 * K_ATOM + a * K_ATOM, &p.v_lo, bar(kVFull), 32 * a, j * KB, h, b);
+            tma_load_4d(base + OFF_V + a * K_ATOM, &p.v_hi, bar(kVFull), 32 * a, key, c.it.h, c.it.b);
+            tma_load_4d(base + OFF_V + 2 * K_ATOM + a * K_ATOM, &p.v_lo, bar(kVFull), 32 * a, key, c.it.h, c.it.b);
           }
         } else {  // V^T: 4 boxes of 32 keys x 64 dims
           for (int a = 0; a < KB / 32; a++) {
-            tma_load_4d(base + OFF_V + a * VT_ATOM, &p.v_hi, bar(kVFull), j * KB + 32 * a, 0, h, b);
-            tma_load_4d(base + OFF_V + V_BYTES / 2 + a * VT_ATOM, &p.v_lo, bar(kVFull), j * KB + 32 * a, 0, h, b);
+            tma_load_4d(base + OFF_V + a * VT_ATOM, &p.v_hi, bar(kVFull), key + 32 * a, 0, c.it.h, c.it.b);
+            tma_load_4d(base + OFF_V + V_BYTES / 2 + a * VT_ATOM, &p.v_lo, bar(kVFull), key + 32 * a, 0, c.it.h,
+                        c.it.b);
           }
         }
       };
-      // K_j is reloaded once S_{j-1} has completed (KEmpty completion j), V_j
-      // once P.V_{j-1} has (VEmpty completion j); this order matches the order
-      // in which the MMA thread needs them.
-      load_k(0);
-      load_v(0);
+      load_k(ck);
+      load_v(cv);
       bool ok = true;
-      if (nb > 1) {
+      if (T > 1) {
         ok = mbar_wait(bar(kKEmpty), 0, p.err, 12);
-        if (ok) load_k(1);
+        ck.next();
+        if (ok) load_k(ck);
       }
-      for (int j = 1; j < nb && ok; j++) {
-        if (j + 1 < nb) {
-          if (!mbar_wait(bar(kKEmpty), j & 1, p.err, 12)) break;
-          load_k(j + 1);
+      for (int t = 1; t < T && ok; t++) {
+        if (t + 1 < T) {
+          if (!mbar_wait(bar(kKEmpty), t & 1, p.err, 12)) break;
+          ck.next();
+          load_k(ck);
         }
-        if (!mbar_wait(bar(kVEmpty), (j - 1) & 1, p.err, 11)) break;
-        load_v(j);
+        if (!mbar_wait(bar(kVEmpty), (t - 1) & 1, p.err, 11)) break;
+        cv.next();
+        load_v(cv);
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && T > 0) {
       // Descriptors are built once per buffer and offset by constants (the
       // start-address field is the low 14 bits of a descriptor, address / 16,
       // so desc(a + o) = desc(a) + o / 16).
@@ -216,11 +278,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
       const uint64_t dvm = make_desc_mn(base + OFF_V);
       const bool mn = p.v_rows != 0;
       const uint32_t idesc_pv = mn ? (IDESC_PV | (1u << 16)) : IDESC_PV;  // B MN-major for V rows
-      bool ok = mbar_wait(bar(kQFull), 0, p.err, 13);
-      auto qk = [&](int j) {  // S_j = Q K_j^T into buffer j & 1
-        if (!mbar_wait(bar(kKFull), j & 1, p.err, 17)) return false;
+      Cursor cq(p);
+      auto qk = [&](int t) {  // S_t = Q K_t^T into buffer t & 1
+        if (cq.j == 0 && !mbar_wait(bar(kQFull), cq.i & 1, p.err, 13)) return false;
+        if (!mbar_wait(bar(kKFull), t & 1, p.err, 17)) return false;
         tc_fence_after();
-        const uint32_t scol = tmem + 128 * (j & 1);
+        const uint32_t scol = tmem + 128 * (t & 1);
 #pragma unroll
         for (int kk = 0; kk < HD / 8; kk++) {
           const uint32_t off = (kk & 3) * 32;
@@ -233,14 +296,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
           mma_tf32(scol, qh, kh, IDESC_QK, 1u);
         }
         mma_commit(bar(kKEmpty));
-        mma_commit(bar(kSFull + (j & 1)));
+        mma_commit(bar(kSFull + (t & 1)));
+        cq.next();
         return true;
       };
-      auto pv = [&](int j) {  // O_j = P_j V_j into buffer j & 1
-        const int u = j & 1;
-        if (!mbar_wait(bar(kPFull), j & 1, p.err, 14)) return false;
-        if (!mbar_wait(bar(kVFull), j & 1, p.err, 15)) return false;
-        if (j >= 2 && !mbar_wait(bar(kOEmpty + u), ((j >> 1) & 1) ^ 1, p.err, 16)) return false;
+      auto pv = [&](int t) {  // O_t = P_t V_t into buffer t & 1
+        const int u = t & 1;
+        if (!mbar_wait(bar(kPFull), t & 1, p.err, 14)) return false;
+        if (!mbar_wait(bar(kVFull), t & 1, p.err, 15)) return false;
+        if (t >= 2 && !mbar_wait(bar(kOEmpty + u), ((t >> 1) & 1) ^ 1, p.err, 16)) return false;
         tc_fence_after();
         const uint32_t phi = tmem + 128 * u, plo = tmem + COL_PLO, ocol = tmem + COL_O + 64 * u;
         const uint64_t dv = mn ? dvm : dv0;
@@ -258,13 +322,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
         mma_commit(bar(kOFull + u));
         return true;
       };
-      if (ok) ok = qk(0);
-      if (ok && nb > 1) ok = qk(1);
-      for (int j = 0; j < nb && ok; j++) {
-        ok = pv(j);
-        // S_{j+2} reuses S_j's columns, which hold P_hi_j: issued after P.V_j,
+      bool ok = qk(0);
+      if (ok && T > 1) ok = qk(1);
+      for (int t = 0; t < T && ok; t++) {
+        ok = pv(t);
+        // S_{t+2} reuses S_t's columns, which hold P_hi_t: issued after P.V_t,
         // and MMAs of one thread run in issue order.
-        if (ok && j + 2 < nb) ok = qk(j + 2);
+        if (ok && t + 2 < T) ok = qk(t + 2);
       }
     }
   } else {
@@ -282,10 +346,78 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
 #pragma unroll
     for (int i = 0; i < HO; i++) o[i] = 0.0f;
     float m = __int_as_float(0xff800000), l = 0.0f, corr_prev = 1.0f;
+    // Where row r of an item's output goes: with a split key axis the row of
+    // its (unit, range) slot in part_o / part_ml, else the element offset of
+    // the row in O (-1: past Sq).
+    auto out_of = [&](const Item &it) -> int64_t {
+      if (p.kv_splits > 1) return (int64_t(it.unit) * p.kv_splits + it.sp) * QT + r;
+      const int row = it.q0 + r;
+      if (row >= p.Sq) return -1;
+      return int64_t(it.b) * p.so_b + int64_t(it.h) * p.so_h + int64_t(row) * p.ldo + HO * hh;
+    };
+    // O = o / l, or with a split key axis this range's o, m, l; written once
+    // the item's last O block is folded in.
+    auto write_out = [&](int64_t dst, float m_it, float l_it) {
+      if (p.kv_splits > 1) {
+        float *po = p.part_o + dst * HD + HO * hh;
+#pragma unroll
+        for (int c = 0; c < HO; c += 4)
+          *reinterpret_cast<float4 *>(po + c) = make_float4(o[c], o[c + 1], o[c + 2], o[c + 3]);
+        if (hh == 0) *reinterpret_cast<float2 *>(p.part_ml + dst * 2) = make_float2(m_it, l_it);
+        return;
+      }
+      if (dst < 0 || *reinterpret_cast<volatile int *>(p.err) != 0) return;
+      const float inv = __frcp_rn(l_it);
+#pragma unroll
+      for (int c = 0; c < HO; c += 4) {
+        float4 v = make_float4(__fmul_rn(o[c], inv), __fmul_rn(o[c + 1], inv), __fmul_rn(o[c + 2], inv),
+                               __fmul_rn(o[c + 3], inv));
+        if (p.O) *reinterpret_cast<float4 *>(p.O + dst + c) = v;
+        if (p.O_hi) {
+          float4 hv = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
+          *reinterpret_cast<float4 *>(p.O_hi + dst + c) = hv;
+          *reinterpret_cast<float4 *>(p.O_lo + dst + c) =
+              make_float4(__fsub_rn(v.x, hv.x), __fsub_rn(v.y, hv.y), __fsub_rn(v.z, hv.z), __fsub_rn(v.w, hv.w));
+        }
+      }
+    };
+    // fold O_t (relative to the max before block t + 1) into o
+    auto fold = [&](int t) {
+      const int u = t & 1;
+      bool w = mbar_wait(bar(kOFull + u), (t >> 1) & 1, p.err, 20);
+      if (!__all_sync(0xffffffffu, w)) return false;
+      tc_fence_after();
+      uint32_t r0[32];
+      tmem_ld32_nowait(lane_base + COL_O + 64 * u + HO * hh, r0);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kOEmpty + u));
+#pragma unroll
+      for (int i = 0; i < HO; i++) o[i] = __fadd_rn(__fmul_rn(o[i], corr_prev), __uint_as_float(r0[i]));
+      return true;
+    };
+    // the current item (its block j of nb from key block kb0) and where
+    // the previous one's rows go
+    int item = blockIdx.x, j = 0, nb = 0, kb0 = 0;
+    int64_t dst_prev = 0, dst = 0;
+    if (T > 0) {
+      const Item it = item_of(p, item);
+      nb = it.nb, kb0 = it.kb0, dst = out_of(it);
+    }
+    float m_prev = m, l_prev = l;
     bool ok = true;
-    for (int j = 0; j < nb; j++) {
-      const int s = j & 1;
-      bool w = mbar_wait(bar(kSFull + s), (j >> 1) & 1, p.err, 19);
+    for (int t = 0; t < T; t++) {
+      const int s = t & 1;
+      if (j == nb) {  // the next item: its row state starts afresh
+        item += gridDim.x;
+        const Item it = item_of(p, item);
+        nb = it.nb, kb0 = it.kb0, j = 0;
+        dst_prev = dst, dst = out_of(it);
+        m_prev = m, l_prev = l;
+        m = __int_as_float(0xff800000), l = 0.0f;
+      }
+      bool w = mbar_wait(bar(kSFull + s), (t >> 1) & 1, p.err, 19);
       if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
       tc_fence_after();
       float sc[HK];
@@ -301,11 +433,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
         }
       }
       float mj = __int_as_float(0xff800000);
-      const bool tail = (j + 1) * KB > p.Sk;
+      const int key0 = (kb0 + j) * KB;
+      const bool tail = key0 + KB > p.Sk;
 #pragma unroll
       for (int i = 0; i < HK; i++) {
         float x = __fmul_rn(sc[i], p.scale);           // the reference's `* scale` node
-        if (tail && j * KB + HK * hh + i >= p.Sk) x = __int_as_float(0xff800000);
+        if (tail && key0 + HK * hh + i >= p.Sk) x = __int_as_float(0xff800000);
         sc[i] = x;
         mj = fmaxf(mj, x);
       }
@@ -322,10 +455,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
       }
       xsum[hh * QT + r] = ps;
       m = m_new;
-      // P_j: hi over this half's scores (already read), lo into the P_lo
-      // columns once P.V_{j-1} has finished reading them.
-      if (j >= 1) {
-        bool w3 = mbar_wait(bar(kPEmpty), (j - 1) & 1, p.err, 22);
+      // P_t: hi over this half's scores (already read), lo into the P_lo
+      // columns once P.V_{t-1} has finished reading them.
+      if (t >= 1) {
+        bool w3 = mbar_wait(bar(kPEmpty), (t - 1) & 1, p.err, 22);
         if (!__all_sync(0xffffffffu, w3)) { ok = false; break; }
         tc_fence_after();
       }
@@ -348,57 +481,68 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
       asm volatile("bar.sync 1, 256;" ::: "memory");
       l = __fadd_rn(__fmul_rn(l, corr), __fadd_rn(xsum[r], xsum[QT + r]));
       if (lane == 0) mbar_arrive(bar(kPFull));
-      if (j >= 1) {  // fold O_{j-1} (relative to the previous max) into o
-        const int u = (j - 1) & 1;
-        bool w2 = mbar_wait(bar(kOFull + u), ((j - 1) >> 1) & 1, p.err, 20);
-        if (!__all_sync(0xffffffffu, w2)) { ok = false; break; }
-        tc_fence_after();
-        uint32_t r0[32];
-        tmem_ld32_nowait(lane_base + COL_O + 64 * u + HO * hh, r0);
-        tmem_ld_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(kOEmpty + u));
+      if (t >= 1) {
+        // O_{t-1}, folded while P.V_t runs; when it closed the previous item,
+        // that item's rows are written and o starts afresh.
+        if (!fold(t - 1)) { ok = false; break; }
+        if (j == 0) {
+          write_out(dst_prev, m_prev, l_prev);
 #pragma unroll
-        for (int i = 0; i < HO; i++) o[i] = __fadd_rn(__fmul_rn(o[i], corr_prev), __uint_as_float(r0[i]));
-      }
-      corr_prev = corr;
-    }
-    if (ok && nb >= 1) {
-      const int u = (nb - 1) & 1;
-      bool w = mbar_wait(bar(kOFull + u), ((nb - 1) >> 1) & 1, p.err, 21);
-      if (__all_sync(0xffffffffu, w)) {
-        tc_fence_after();
-        uint32_t r0[32];
-        tmem_ld32_nowait(lane_base + COL_O + 64 * u + HO * hh, r0);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < HO; i++) o[i] = __fadd_rn(__fmul_rn(o[i], corr_prev), __uint_as_float(r0[i]));
-        const int row = q0 + r;
-        if (row < p.Sq && *reinterpret_cast<volatile int *>(p.err) == 0) {
-          const float inv = __frcp_rn(l);
-          const int64_t off = int64_t(b) * p.so_b + int64_t(h) * p.so_h + int64_t(row) * p.ldo + HO * hh;
-#pragma unroll
-          for (int c = 0; c < HO; c += 4) {
-            float4 v = make_float4(__fmul_rn(o[c], inv), __fmul_rn(o[c + 1], inv), __fmul_rn(o[c + 2], inv),
-                                   __fmul_rn(o[c + 3], inv));
-            if (p.O) *reinterpret_cast<float4 *>(p.O + off + c) = v;
-            if (p.O_hi) {
-              float4 hv = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
-              *reinterpret_cast<float4 *>(p.O_hi + off + c) = hv;
-              *reinterpret_cast<float4 *>(p.O_lo + off + c) =
-                  make_float4(__fsub_rn(v.x, hv.x), __fsub_rn(v.y, hv.y), __fsub_rn(v.z, hv.z), __fsub_rn(v.w, hv.w));
-            }
-          }
+          for (int i = 0; i < HO; i++) o[i] = 0.0f;
         }
       }
+      corr_prev = corr;
+      j++;
     }
+    if (ok && T > 0 && fold(T - 1)) write_out(dst, m, l);
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+  }
+}
+
+// Output of a split-KV launch: per query row, the shares of the S key ranges
+// (O_s relative to its max m_s, sum l_s) rescaled to the common max:
+// O = sum_s O_s e^(m_s - M) / sum_s l_s e^(m_s - M), ranges added in order.
+// A thread = 4 output columns of one row.
+__global__ void __launch_bounds__(256) attn_combine(const AttnParams p) {
+  const int64_t g = int64_t(blockIdx.x) * 256 + threadIdx.x;
+  const int c4 = int(g % (HD / 4)), r = int((g / (HD / 4)) % QT);
+  const int unit = int(g / (HD / 4) / QT);
+  if (unit >= p.units || *reinterpret_cast<volatile int *>(p.err) != 0) return;
+  const int qt = unit % p.tiles_q, bh = unit / p.tiles_q;
+  const int h = bh % p.heads, b = bh / p.heads;
+  const int row = qt * QT + r;
+  if (row >= p.Sq) return;
+  const int S = p.kv_splits;
+  float M = __int_as_float(0xff800000);
+  for (int s = 0; s < S; s++) M = fmaxf(M, p.part_ml[((size_t(unit) * S + s) * QT + r) * 2]);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float L = 0.0f;
+  for (int s = 0; s < S; s++) {
+    const size_t slot = size_t(unit) * S + s;
+    const float2 ml = *reinterpret_cast<const float2 *>(p.part_ml + (slot * QT + r) * 2);
+    const float w = (ml.x == M) ? 1.0f : exp_ex2(__fsub_rn(ml.x, M));
+    const float4 o = *reinterpret_cast<const float4 *>(p.part_o + (slot * QT + r) * HD + 4 * c4);
+    acc.x = __fadd_rn(acc.x, __fmul_rn(o.x, w));
+    acc.y = __fadd_rn(acc.y, __fmul_rn(o.y, w));
+    acc.z = __fadd_rn(acc.z, __fmul_rn(o.z, w));
+    acc.w = __fadd_rn(acc.w, __fmul_rn(o.w, w));
+    L = __fadd_rn(L, __fmul_rn(ml.y, w));
+  }
+  const float inv = __frcp_rn(L);
+  const float4 v = make_float4(__fmul_rn(acc.x, inv), __fmul_rn(acc.y, inv), __fmul_rn(acc.z, inv),
+                               __fmul_rn(acc.w, inv));
+  const int64_t off = int64_t(b) * p.so_b + int64_t(h) * p.so_h + int64_t(row) * p.ldo + 4 * c4;
+  if (p.O) *reinterpret_cast<float4 *>(p.O + off) = v;
+  if (p.O_hi) {
+    const float4 hv = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
+    *reinterpret_cast<float4 *>(p.O_hi + off) = hv;
+    *reinterpret_cast<float4 *>(p.O_lo + off) =
+        make_float4(__fsub_rn(v.x, hv.x), __fsub_rn(v.y, hv.y), __fsub_rn(v.z, hv.z), __fsub_rn(v.w, hv.w));
   }
 }
 
@@ -411,7 +555,45 @@ bool view_ok(const void *p, int64_t ld, int64_t sb, int64_t sh) {
 
 using namespace silcu;
 
-extern "C" silcu_status silcu_attention_f32(const silcu_attention_args *ap, silcu_stream stream) {
+namespace {
+
+// Key-range split per (batch, head, query tile) for a launch of U such
+// units over nbt key blocks on the SMs (one CTA per SM): modelled time
+// waves(U*S) * (ceil(nbt/S) + 1 block of fixed cost) plus the combine pass
+// (about one block); a split is taken only when the model gains 15 %.
+int choose_kv_splits(int64_t U, int64_t nbt) {
+  const int64_t sms = sm_count();
+  auto cost = [&](int64_t S) {
+    const int64_t waves = (U * S + sms - 1) / sms;
+    return double(waves * ((nbt + S - 1) / S + 1)) + (S > 1 ? 1.0 : 0.0);
+  };
+  int best = 1;
+  double bc = cost(1);
+  for (int64_t S = 2; S <= 4 && S <= nbt; S++) {
+    const double c = cost(S);
+    if (c < 0.85 * bc && c < cost(best)) best = int(S);
+  }
+  return best;
+}
+
+int64_t splits_for(const silcu_attention_args &a) {
+  if (a.Sq <= 0 || a.Sk <= 0 || a.batch <= 0 || a.heads <= 0) return 1;
+  const int64_t U = (a.Sq + QT - 1) / QT * a.heads * a.batch;
+  const int64_t nbt = (a.Sk + KB - 1) / KB;
+  if (const char *e = getenv("SILCU_ATTN_SPLITS")) {  // tuning override, clamped to [1, min(4, nbt)]
+    const int64_t S = atoi(e);
+    return S < 1 ? 1 : S > 4 ? 4 : S > nbt ? nbt : S;
+  }
+  return choose_kv_splits(U, nbt);
+}
+
+size_t split_ws_bytes(int64_t U, int64_t S) {
+  if (S <= 1) return 0;
+  return size_t(U) * S * QT * (HD + 2) * sizeof(float) + 256;
+}
+
+silcu_status attention_launch(const silcu_attention_args *ap, int64_t S, void *ws, size_t wsb,
+                              silcu_stream stream) {
   if (!ap) return fail(SILCU_INVALID_ARGUMENT, "attention: null args");
   const silcu_attention_args &a = *ap;
   if (a.D != HD) return fail(SILCU_UNSUPPORTED, "attention: head dimension %lld (only 64)", (long long)a.D);
@@ -466,6 +648,49 @@ extern "C" silcu_status silcu_attention_f32(const silcu_attention_args *ap, silc
     if (e != cudaSuccess) return fail(SILCU_CUDA_ERROR, "attention: smem attribute: %s", cudaGetErrorString(e));
     configured[dev] = true;
   }
-  attn_kernel<<<uint32_t(tiles_q * a.heads * a.batch), NUM_THREADS, SMEM_BYTES, as_stream(stream)>>>(p);
-  return check_launch("attention");
+  const int64_t U = tiles_q * a.heads * a.batch;
+  const int64_t nbt = (a.Sk + KB - 1) / KB;
+  if (S < 1 || S > nbt || U * S > 0x7FFFFFFF) S = 1;
+  p.kv_splits = int(S);
+  p.units = int(U);
+  p.items = int(U * S);
+  if (S > 1) {
+    const size_t need = split_ws_bytes(U, S);
+    if (!ws || wsb < need) return fail(SILCU_WORKSPACE_TOO_SMALL, "attention: workspace %zu < %zu", wsb, need);
+    if (!aligned16(ws)) return fail(SILCU_INVALID_ARGUMENT, "attention: workspace not 16-byte aligned");
+    p.part_o = static_cast<float *>(ws);
+    p.part_ml = p.part_o + size_t(U) * S * QT * HD;
+  }
+  // persistent: one CTA per SM, items dealt round-robin
+  const int64_t grid = U * S < sm_count() ? U * S : sm_count();
+  attn_kernel<<<uint32_t(grid), NUM_THREADS, SMEM_BYTES, as_stream(stream)>>>(p);
+  silcu_status r = check_launch("attention");
+  if (r != SILCU_OK || S == 1) return r;
+  const int64_t threads = U * QT * (HD / 4);
+  attn_combine<<<uint32_t((threads + 255) / 256), 256, 0, as_stream(stream)>>>(p);
+  return check_launch("attention(combine)");
 }
+
+}  // namespace
+
+extern "C" {
+
+silcu_status silcu_attention_f32(const silcu_attention_args *args, silcu_stream stream) {
+  return attention_launch(args, 1, nullptr, 0, stream);
+}
+
+size_t silcu_attention_workspace_bytes(const silcu_attention_args *args) {
+  if (!args) return 0;
+  const int64_t S = splits_for(*args);
+  const int64_t U = (args->Sq + QT - 1) / QT * args->heads * args->batch;
+  return split_ws_bytes(U, S);
+}
+
+silcu_status silcu_attention_ex(const silcu_attention_args *args, void *ws, size_t wsb, silcu_stream stream) {
+  if (!args) return fail(SILCU_INVALID_ARGUMENT, "attention: null args");
+  int64_t S = splits_for(*args);
+  if (S > 1 && wsb < split_ws_bytes((args->Sq + QT - 1) / QT * args->heads * args->batch, S)) S = 1;
+  return attention_launch(args, S, ws, wsb, stream);
+}
+
+}  // extern "C"

@@ -314,7 +314,8 @@ def attention(Q, K, Vt, *, Sq, Sk, batch, heads, ldq, sq_b, sq_h, ldk, sk_b, sk_
     a.so_h = Sq * D if so_h is None else so_h
     a.so_b = heads * Sq * D if so_b is None else so_b
     a.scale = float(scale)
-    check(lib().silcu_attention_f32(ct.byref(a), _stream()))
+    wp, wn = _ws_args(lib().silcu_attention_workspace_bytes(ct.byref(a)), Q[0].device)
+    check(lib().silcu_attention_ex(ct.byref(a), wp, wn, _stream()))
     return O
 
 

@@ -69,3 +69,60 @@ def test_attention_v_rows(cuda, B, H, S):
             assert_dot_close(got[b, h], _ref(q[b, h], k[b, h], v[b, h], np.float32(0.125)), S,
                              what=f"attention (V rows) b{b} h{h}")
     gpu.device_status()
+
+
+def _attn_inputs(B, H, Sq, Sk, seed):
+    D = 64
+    rng = np.random.default_rng(seed)
+    q = rng.normal(0, 1, (B, H, Sq, D)).astype(np.float32)
+    k = rng.normal(0, 1, (B, H, Sk, D)).astype(np.float32)
+    v = rng.normal(0, 1, (B, H, Sk, D)).astype(np.float32)
+    return q, k, v
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 4])
+@pytest.mark.parametrize("B,H,Sq,Sk", [(2, 3, 200, 700), (1, 2, 128, 1024), (1, 1, 64, 300)])
+def test_attention_split_kv(cuda, monkeypatch, splits, B, H, Sq, Sk):
+    """Split-KV: each (batch, head, query tile) as up to 4 key ranges on
+    separate CTAs plus the combine pass, forced by SILCU_ATTN_SPLITS, ragged
+    Sq and Sk (tail key block inside the last range).  Within the chain's
+    tolerance of the oracle; the split output (hi + lo) equals the plain
+    output; one range is the unsplit kernel bit for bit."""
+    D = 64
+    q, k, v = _attn_inputs(B, H, Sq, Sk, Sq + Sk + splits)
+    dq, dk, dv = (torch.from_numpy(t).cuda().reshape(-1) for t in (q, k, v))
+    qs = gpu.split(dq, B * H * Sq, D)
+    ks = gpu.split(dk, B * H * Sk, D)
+    vs = gpu.split(dv, B * H * Sk, D)
+    common = dict(Sq=Sq, Sk=Sk, batch=B, heads=H, ldq=D, sq_b=H * Sq * D, sq_h=Sq * D, ldk=D, sk_b=H * Sk * D,
+                  sk_h=Sk * D, scale=float(np.float32(0.125)), ldv=D, sv_b=H * Sk * D, sv_h=Sk * D)
+    monkeypatch.setenv("SILCU_ATTN_SPLITS", "1")
+    o1 = gpu.attention(qs, ks, None, V=vs, **common)
+    monkeypatch.setenv("SILCU_ATTN_SPLITS", str(splits))
+    hi = torch.empty(B * H * Sq * D, device="cuda")
+    lo = torch.empty_like(hi)
+    o = gpu.attention(qs, ks, None, V=vs, O=torch.empty_like(hi), O_split=(hi, lo), **common)
+    torch.cuda.synchronize()
+    got = o.cpu().numpy().reshape(B, H, Sq, D)
+    np.testing.assert_array_equal((hi + lo).cpu().numpy().reshape(B, H, Sq, D), got)
+    if splits == 1:
+        np.testing.assert_array_equal(got, o1.cpu().numpy().reshape(B, H, Sq, D))
+    for b in range(B):
+        for h in range(H):
+            r = _ref(q[b, h], k[b, h], v[b, h], np.float32(0.125))
+            assert_dot_close(got[b, h], r, Sk, what=f"split {splits} attention b{b} h{h}")
+    gpu.device_status()
+
+
+def test_attention_split_choice(cuda, monkeypatch):
+    """The split is taken by shape: one query tile over 4096 keys splits (a
+    workspace is asked for); the benchmark's 12 heads x 4 query tiles x batch
+    32 does not."""
+    import ctypes as ct
+    from silarray_b200 import _lib
+    monkeypatch.delenv("SILCU_ATTN_SPLITS", raising=False)
+    a = _lib.AttnArgs()
+    a.Sq, a.Sk, a.D, a.batch, a.heads = 128, 4096, 64, 1, 1
+    assert gpu.lib().silcu_attention_workspace_bytes(ct.byref(a)) > 0
+    a.Sq, a.Sk, a.batch, a.heads = 512, 512, 32, 12
+    assert gpu.lib().silcu_attention_workspace_bytes(ct.byref(a)) == 0
