@@ -43,8 +43,9 @@ def parse():
     ap.add_argument("--no-suite", action="store_true", help="skip the per-configuration suite in the headline line")
     ap.add_argument("--suite", action="store_true",
                     help="measure every configuration of the metric (one JSON line each) instead of the headline")
-    ap.add_argument("--profile-case", default=None, choices=["gemm", "block", "attention", "hbm", "sgemm"],
-                    help="run only a small case for ncu: the FFN-up GEMM of the workload, or a 2-sequence block")
+    ap.add_argument("--profile-case", default=None, choices=["gemm", "block", "shard", "attention", "hbm", "sgemm"],
+                    help="run only a small case for ncu: the FFN-up GEMM of the workload, a 2-sequence block, "
+                         "or the 8-GPU per-rank forward (4 sequences)")
     return ap.parse_args()
 
 
@@ -67,6 +68,7 @@ def profile_case(args):
     """Small, self-terminating cases for ncu captures (one GPU): `gemm` runs the
     dominant kernel as the forward does (FFN-up, M=16384 N=3072 K=768, ~600 MB
     on the device) warmup+1 times; `block` runs a 2-sequence transformer forward;
+    `shard` the 8-GPU per-rank forward (4 sequences, ~200 MB);
     `attention` the fused attention on a quarter of the BMM-attention config;
     `hbm` the HBM-bound kernels of the suite once each after the warm-ups
     (GEMV 1x4096.4096x4096, small batch 32x4096.4096x768, softmax /
@@ -118,7 +120,7 @@ def profile_case(args):
             gpu.argmax_f32(r32, rows=4096, cols=32768)
             gpu.sum_f32(flat)
     else:
-        cfg = transformer.Config(batch=2)
+        cfg = transformer.Config(batch=4 if args.profile_case == "shard" else 2)
         blk = transformer.Block(cfg, transformer.init_params(cfg), device=dev)
         x = torch.from_numpy(transformer.init_input(cfg)).to(dev)
         for _ in range(args.warmup + 1):
