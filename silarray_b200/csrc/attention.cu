@@ -51,10 +51,13 @@ constexpr int V_BYTES = 2 * HD * KB * 4;    // hi, lo of 64 x 128 = 64 KB
 constexpr int OFF_Q = 0, OFF_K = Q_BYTES, OFF_V = OFF_K + K_BYTES;
 constexpr int DATA_BYTES = OFF_V + V_BYTES;  // 192 KB of 1024-aligned operand buffers
 // Ahead of them: the mbarriers + the TMEM slot (256 B) and the row max / sum
-// exchange between the two softmax halves (2 x 2 x 128 floats).
-constexpr int HEAD_BYTES = 256 + 2 * 2 * QT * 4;
+// exchange between the softmax warps of a lane quarter (2 x ESPLIT x 128 floats).
+// Softmax warps per TMEM lane quarter; each takes 1/ESPLIT of a block's keys
+// and of the output columns.
+constexpr int ESPLIT = 2;
+constexpr int HEAD_BYTES = 256 + 2 * ESPLIT * QT * 4;
 constexpr int SMEM_BYTES = 232448;  // the per-CTA maximum; the data start is aligned up past HEAD_BYTES
-constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter: keys / output columns split in halves
+constexpr int EPI_WARPS = 4 * ESPLIT;
 constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
 // TMEM columns: S_j (then P_hi_j) in [128*(j&1), +128), P_lo in [256, 384),
 // O_j in [384 + 64*(j&1), +64).
@@ -166,6 +169,26 @@ __device__ __forceinline__ float exp_ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(__fmul_rn(x, kLog2e)));
   return y;
+}
+
+// TMEM load of N (16 or 32, or 64 as two 32s) consecutive columns of this warp's lanes.
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t *r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]) {
+  static_assert(N == 16 || N % 32 == 0, "16 or a multiple of 32 columns");
+  if constexpr (N == 16) {
+    tmem_ld16_nowait(taddr, r);
+  } else {
+#pragma unroll
+    for (int c = 0; c < N; c += 32) tmem_ld32_nowait(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(r + c));
+  }
 }
 
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -338,10 +361,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
     const int q = warp & 3;
     const int hh = (warp - 2) >> 2;
     const int r = 32 * q + lane;
-    float *xmax = xch;                                         // [2][QT]
-    float *xsum = xmax + 2 * QT;                               // [2][QT]
+    float *xmax = xch;                                         // [ESPLIT][QT]
+    float *xsum = xmax + ESPLIT * QT;                          // [ESPLIT][QT]
     const uint32_t lane_base = tmem + (uint32_t(32 * q) << 16);
-    constexpr int HK = KB / 2, HO = HD / 2;
+    constexpr int HK = KB / ESPLIT, HO = HD / ESPLIT;
     float o[HO];
 #pragma unroll
     for (int i = 0; i < HO; i++) o[i] = 0.0f;
@@ -387,8 +410,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
       bool w = mbar_wait(bar(kOFull + u), (t >> 1) & 1, p.err, 20);
       if (!__all_sync(0xffffffffu, w)) return false;
       tc_fence_after();
-      uint32_t r0[32];
-      tmem_ld32_nowait(lane_base + COL_O + 64 * u + HO * hh, r0);
+      uint32_t r0[HO];
+      tmem_ld_cols<HO>(lane_base + COL_O + 64 * u + HO * hh, r0);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
@@ -422,15 +445,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
       tc_fence_after();
       float sc[HK];
       {
-        uint32_t r0[32], r1[32];
-        tmem_ld32_nowait(lane_base + 128 * s + HK * hh, r0);
-        tmem_ld32_nowait(lane_base + 128 * s + HK * hh + 32, r1);
+        uint32_t r0[HK];
+        tmem_ld_cols<HK>(lane_base + 128 * s + HK * hh, r0);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; i++) {
-          sc[i] = __uint_as_float(r0[i]);
-          sc[32 + i] = __uint_as_float(r1[i]);
-        }
+        for (int i = 0; i < HK; i++) sc[i] = __uint_as_float(r0[i]);
       }
       float mj = __int_as_float(0xff800000);
       const int key0 = (kb0 + j) * KB;
@@ -443,8 +462,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
         mj = fmaxf(mj, x);
       }
       xmax[hh * QT + r] = mj;
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      const float m_new = fmaxf(m, fmaxf(xmax[r], xmax[QT + r]));
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * EPI_WARPS) : "memory");
+      float m_new = m;
+#pragma unroll
+      for (int e = 0; e < ESPLIT; e++) m_new = fmaxf(m_new, xmax[e * QT + r]);
       const float corr = (m == m_new) ? 1.0f : exp_ex2(__fsub_rn(m, m_new));
       float ps = 0.0f;
 #pragma unroll
@@ -478,8 +499,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
       }
       tmem_st_wait();
       tc_fence_before();
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      l = __fadd_rn(__fmul_rn(l, corr), __fadd_rn(xsum[r], xsum[QT + r]));
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * EPI_WARPS) : "memory");
+      float ls = xsum[r];
+#pragma unroll
+      for (int e = 1; e < ESPLIT; e++) ls = __fadd_rn(ls, xsum[e * QT + r]);
+      l = __fadd_rn(__fmul_rn(l, corr), ls);
       if (lane == 0) mbar_arrive(bar(kPFull));
       if (t >= 1) {
         // O_{t-1}, folded while P.V_t runs; when it closed the previous item,
