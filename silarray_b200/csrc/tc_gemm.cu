@@ -701,16 +701,21 @@ silcu_status launch_tc(const TcParams &p, uint32_t grid, cudaStream_t s) {
   return check_launch("sgemm(tc)");
 }
 
-// CTA pairs (256-row tiles) when there are enough of them to occupy every
-// SM pair; SILCU_TC_PAIR = 0 / 1 forces the choice (tuning).
-bool use_pair(int64_t M, int64_t tiles_n, int64_t nb) {
+// CTA pairs (256-row tiles) when they occupy nearly every SM pair (90 %), or
+// when K is long (>= 2048), where the halved B traffic per CTA pays even with
+// split-K filling the grid: measured at M = 2048 / 4096, N = 768, K = 3072
+// 59.2 -> 54.8 / 103.3 -> 94.7 us, and QKV (M = 2048, N = 2304, K = 768, 72
+// pair tiles) 47.2 -> 45.8 us; at K = 768 with few tiles (N = 768, M = 4096)
+// single CTAs stay ahead (38.2 vs 40.0 us).  SILCU_TC_PAIR = 0 / 1 forces the
+// choice (tuning).
+bool use_pair(int64_t M, int64_t tiles_n, int64_t nb, int64_t K) {
   static const int forced = [] {
     const char *e = getenv("SILCU_TC_PAIR");
     return e ? atoi(e) : -1;
   }();
   if (forced == 0 || forced == 1) return forced == 1 && M >= 2 * BM;
   const int64_t pair_tiles = (M + 2 * BM - 1) / (2 * BM) * tiles_n * nb;
-  return M >= 2 * BM && pair_tiles >= sm_count() / 2;
+  return M >= 2 * BM && (10 * pair_tiles >= 9 * (sm_count() / 2) || K >= 2048);
 }
 
 // Tile width: the widest that N needs.  Narrower tiles never pay for a
@@ -763,7 +768,7 @@ TcPlan tc_plan(const silcu_gemm_args &a) {
   TcPlan pl;
   const int64_t Kp = padded_k(a.K > 0 ? a.K : 1);
   const int64_t nb = total_batch(a);
-  pl.pair = use_pair(a.M, (a.N + 255) / 256, nb);
+  pl.pair = use_pair(a.M, (a.N + 255) / 256, nb, a.K);
   pl.BN = pick_bn(a.N);
   pl.TM = pl.pair ? 2 * BM : BM;
   pl.tiles_n = (a.N + pl.BN - 1) / pl.BN;

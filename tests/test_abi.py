@@ -106,20 +106,23 @@ def _visible_sms():
 
 
 def test_gemm_plan_split_k_choice(lib):
+    """The 3xTF32 path's tiling and split-K choice on a 148-SM B200 (the
+    library assumes 148 SMs when it cannot query a device) for the
+    transformer's GEMMs: at a 4-sequence shard (M = 2048) Wo splits every
+    single-CTA tile in 3 K parts, FFN-down (K = 3072) runs CTA pairs with every
+    tile in 3 parts, QKV's 72 pair tiles run whole and FFN-up splits only its
+    last wave's 22 pair tiles; at the full batch (M = 16384) FFN-down splits
+    its last wave's 44 tiles in 5 parts, the other GEMMs none."""
     if _visible_sms() != 148:
         pytest.skip("the pinned plans are those of a 148-SM B200; this device has another SM count")
-    """The 3xTF32 path's split-K choice on a 148-SM B200 (the library assumes
-    148 SMs when it cannot query a device) for the transformer's GEMMs: at a
-    4-sequence shard (M = 2048) the N = 768 GEMMs split every tile in 3 K
-    parts and FFN-up splits only its last wave's 22 pair tiles; at the full
-    batch (M = 16384) FFN-down splits its last wave's 44 tiles in 5 parts,
-    the other GEMMs none."""
     p = _plan(lib, 2048, 768, 768, residual=True)  # Wo
     assert (p.path, p.pair, p.tile_n, p.ksplit, p.tiles, p.whole_tiles) == (2, 0, 256, 3, 48, 0)
+    p = _plan(lib, 2048, 2304, 768, c=False, split_out=True)  # QKV, split output
+    assert (p.pair, p.ksplit, p.tiles, p.whole_tiles) == (1, 1, 72, 72)
     p = _plan(lib, 2048, 3072, 768, c=False, split_out=True)  # FFN-up, split output
     assert (p.pair, p.ksplit, p.tiles, p.whole_tiles) == (1, 3, 96, 74)
     p = _plan(lib, 2048, 768, 3072, residual=True)  # FFN-down
-    assert (p.pair, p.ksplit, p.whole_tiles) == (0, 3, 0)
+    assert (p.pair, p.ksplit, p.tiles, p.whole_tiles) == (1, 3, 24, 0)
     p = _plan(lib, 16384, 768, 3072, residual=True)  # FFN-down, full batch
     assert (p.pair, p.ksplit, p.tiles, p.whole_tiles) == (1, 5, 192, 148)
     for M, N, K in [(16384, 2304, 768), (16384, 3072, 768), (16384, 768, 768)]:
