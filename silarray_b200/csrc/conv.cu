@@ -21,6 +21,7 @@
 #include <string.h>
 
 #include "common.cuh"
+#include "gemm_internal.cuh"
 #include "tc_common.cuh"
 
 namespace silcu {
@@ -40,6 +41,15 @@ ConvShape conv_shape(uint32_t N, uint32_t H, uint32_t W, uint32_t C_in, uint32_t
 }
 
 bool conv_tc(const ConvShape &s) { return s.C_out % 4 == 0 && s.M >= 64 && s.C_out >= 32 && s.Kd >= 16; }
+
+// Implicit GEMM (no patch matrix): the input is split once (hi / lo, NHWC)
+// and the GEMM's A tiles are im2col TMA boxes of it, 16 channels of one
+// filter tap per K block, so C_in must be a multiple of 16.
+bool conv_implicit(const ConvShape &s) {
+  return s.C % 16 == 0 && s.C_out % 4 == 0 && s.M >= 128 && s.C_out >= 32 && s.M * s.C <= int64_t(65535) * 32 * 4096;
+}
+
+size_t conv_split_bytes(const ConvShape &s) { return (size_t(2) * s.M * s.C * sizeof(float) + 255) / 256 * 256; }
 
 // One thread per 4 consecutive patch columns of one output pixel (a float4
 // of hi and of lo when C_in % 4 == 0); columns past K_dim up to the padded
@@ -137,7 +147,17 @@ size_t silcu_conv2d_workspace_bytes(uint32_t N, uint32_t H, uint32_t W, uint32_t
     a.B = reinterpret_cast<const float *>(16);
   }
   patch = (patch + 255) / 256 * 256;
-  return patch + silcu_sgemm_workspace_bytes(&a);
+  size_t need = patch + silcu_sgemm_workspace_bytes(&a);
+  if (conv_implicit(s)) {  // the implicit path: split input + the GEMM's B split / partials
+    silcu_gemm_args g = conv_gemm_args(s, reinterpret_cast<const float *>(16), reinterpret_cast<float *>(16));
+    g.A_hi = g.A_lo = reinterpret_cast<const float *>(16);
+    g.K = s.Kd;
+    g.lda = s.Kd;
+    g.algo = SILCU_GEMM_TC3XTF32;
+    const size_t imp = conv_split_bytes(s) + silcu_sgemm_workspace_bytes(&g);
+    if (imp > need) need = imp;
+  }
+  return need;
 }
 
 silcu_status silcu_conv2d_f32(const float *input, const float *weight, float *output, uint32_t N, uint32_t H,
@@ -152,6 +172,25 @@ silcu_status silcu_conv2d_f32(const float *input, const float *weight, float *ou
   const size_t need = silcu_conv2d_workspace_bytes(N, H, W, C_in, K, C_out);
   if (!ws || wsb < need) return fail(SILCU_WORKSPACE_TOO_SMALL, "conv2d: workspace %zu < %zu", wsb, need);
   cudaStream_t st = as_stream(stream);
+  if (conv_implicit(s) && aligned16(input) && aligned16(output) && aligned16(weight) && s.Kd % 4 == 0) {
+    uint8_t *w8 = static_cast<uint8_t *>(ws);
+    float *hi = reinterpret_cast<float *>(w8);
+    float *lo = hi + s.M * s.C;
+    silcu_status r = silcu_split_f32(input, size_t(s.M), size_t(s.C), size_t(s.C), 0, hi, lo, stream);
+    if (r != SILCU_OK) return r;
+    silcu_gemm_args a = conv_gemm_args(s, weight, output);
+    a.A_hi = hi;
+    a.A_lo = lo;
+    a.K = s.Kd;
+    a.lda = s.Kd;
+    a.algo = SILCU_GEMM_TC3XTF32;
+    TcConv cv;
+    cv.in_hi = hi;
+    cv.in_lo = lo;
+    cv.N = s.N, cv.H = s.H, cv.W = s.W, cv.C = s.C, cv.Kf = s.K, cv.pad = s.pad;
+    const size_t sb = conv_split_bytes(s);
+    return tc_run(a, w8 + sb, wsb - sb, st, &cv);
+  }
   const bool tc = conv_tc(s);
   const bool vec = (s.C % 4 == 0) && aligned16(input);
   uint8_t *w8 = static_cast<uint8_t *>(ws);

@@ -30,7 +30,16 @@ silcu_status skinny_tma_run(const silcu_gemm_args &a, const SkinnyEpi &epi, cuda
 
 // Workspace of the 3xTF32 path: the hi/lo split operands, K-major.
 size_t tc_workspace_bytes(const silcu_gemm_args &a);
-silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t ws_bytes, cudaStream_t s);
+// Implicit-GEMM convolution operand: the exact tf32 split of an NHWC input
+// [N, H, W, C] (C % 16 == 0, 16-byte aligned), read by im2col TMA boxes as
+// the A operand of a GEMM with M = N*H*W rows and K = Kf*Kf*C in (kh, kw, c)
+// order (stride 1, zero padding pad).
+struct TcConv {
+  const float *in_hi, *in_lo;
+  int64_t N, H, W, C, Kf, pad;
+};
+silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t ws_bytes, cudaStream_t s,
+                    const TcConv *conv = nullptr);
 // The 3xTF32 path's tiling and split-K choice for these arguments.
 void tc_describe(const silcu_gemm_args &a, silcu_gemm_plan *out);
 

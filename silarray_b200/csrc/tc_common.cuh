@@ -80,6 +80,30 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map
       : "memory");
 }
 
+// im2col load of a 4-D NHWC tensor {C, W, H, N}: pixelsPerColumn pixels
+// walked in W, H, N order from the base pixel (w, h, n) inside the map's
+// bounding box, channelsPerPixel channels from c, each pixel shifted by the
+// filter tap (kw, kh); pixels outside the tensor read zeros.
+__device__ __forceinline__ void tma_load_im2col(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c, int w,
+                                                int h, int n, uint16_t kw, uint16_t kh) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c), "r"(w), "r"(h), "r"(n), "h"(kw), "h"(kh)
+      : "memory");
+}
+
+// The same for a CTA pair (tcgen05 cta_group::2): completes on `bar`, which
+// may be the pair leader's barrier.
+__device__ __forceinline__ void tma_load_im2col_pair(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c,
+                                                     int w, int h, int n, uint16_t kw, uint16_t kh) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c), "r"(w), "r"(h), "r"(n), "h"(kw), "h"(kh)
+      : "memory");
+}
+
 // CTA-pair form (tcgen05 cta_group::2): the box lands in this CTA's shared
 // memory; the byte count completes on `bar`, a shared::cluster address that
 // may be the pair leader's barrier.
@@ -274,6 +298,35 @@ inline bool make_map4(CUtensorMap *m, const float *base, int64_t inner, int64_t 
                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+typedef CUresult (*EncodeIm2colFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const int *, const int *, cuuint32_t, cuuint32_t,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// An fp32 NHWC tensor as the im2col source of a stride-1 convolution with
+// padding pad on every side: the base pixels of the outputs span
+// [-pad, extent - 1 - pad] in W and H (bounding-box corners -pad, -pad);
+// boxes of `pixels` pixels x `channels` channels.
+inline bool make_im2col_map(CUtensorMap *m, const float *base, int64_t N, int64_t H, int64_t W, int64_t C, int pad,
+                            int channels, int pixels, CUtensorMapSwizzle swz) {
+  static EncodeIm2colFn fn = nullptr;
+  if (!fn) {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeIm2colFn>(ptr);
+  }
+  if (!fn) return false;
+  cuuint64_t dims[4] = {cuuint64_t(C), cuuint64_t(W), cuuint64_t(H), cuuint64_t(N)};
+  cuuint64_t strides[3] = {cuuint64_t(C) * 4, cuuint64_t(W * C) * 4, cuuint64_t(H * W * C) * 4};
+  int lower[2] = {-pad, -pad}, upper[2] = {-pad, -pad};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float *>(base), dims, strides, lower, upper,
+            cuuint32_t(channels), cuuint32_t(pixels), es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 inline bool aligned_view(const void *p, int64_t ld, int64_t s_in, int64_t s_out) {

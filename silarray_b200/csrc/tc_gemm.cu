@@ -101,6 +101,11 @@ struct __align__(64) TcParams {
   // runs in tile_finish).  full_items = all tiles when nothing is split.
   int full_items, ksplit;
   int tma_c, split_out, tma_r;
+  // Implicit-GEMM convolution (conv != 0): A's rows are the output pixels of
+  // an NHWC image batch [images, cv_H, cv_W, cv_C] and its K index runs over
+  // (kh, kw, channel); a_hi / a_lo are im2col maps of the split input, and
+  // each K block (16 channels of one filter tap) loads as one im2col box.
+  int conv, cv_H, cv_W, cv_C, cv_K, cv_pad;
   TcEpi epi;
   int *err;
 };
@@ -251,18 +256,42 @@ __global__ void __launch_bounds__(Cfg<BN_>::NUM_THREADS, 1) tc_gemm_kernel(const
           const uint32_t full = full0 + 8 * s;
           const uint32_t dst = smem_u32(smem + s * STAGE_BYTES);
           const int kc = kb * BK;
+          // im2col coordinates of this K block (convolution): filter tap and
+          // channel offset, and the base input pixel of the tile's first row
+          int cx = 0, cw = 0, ch = 0, cn = 0;
+          uint16_t okw = 0, okh = 0;
+          if (p.conv) {
+            const int tap = kc / p.cv_C;
+            cx = kc - tap * p.cv_C;
+            okh = uint16_t(tap / p.cv_K);
+            okw = uint16_t(tap - int(okh) * p.cv_K);
+            cn = am / (p.cv_H * p.cv_W);
+            const int r = am - cn * (p.cv_H * p.cv_W);
+            ch = r / p.cv_W - p.cv_pad;
+            cw = r % p.cv_W - p.cv_pad;
+          }
           if (PAIR) {
             // Both CTAs' bytes complete on the even CTA's barrier, which expects them all.
             const uint32_t full_c = mapa_shared(full, 0);
             if (rank == 0) mbar_expect_tx(full, 2 * STAGE_BYTES);
-            tma_load_4d_pair(dst, &p.a_hi, full_c, kc, am, bi, bo);
-            tma_load_4d_pair(dst + TILE_A, &p.a_lo, full_c, kc, am, bi, bo);
+            if (p.conv) {
+              tma_load_im2col_pair(dst, &p.a_hi, full_c, cx, cw, ch, cn, okw, okh);
+              tma_load_im2col_pair(dst + TILE_A, &p.a_lo, full_c, cx, cw, ch, cn, okw, okh);
+            } else {
+              tma_load_4d_pair(dst, &p.a_hi, full_c, kc, am, bi, bo);
+              tma_load_4d_pair(dst + TILE_A, &p.a_lo, full_c, kc, am, bi, bo);
+            }
             tma_load_4d_pair(dst + 2 * TILE_A, &p.b_hi, full_c, kc, bn, bi, bo);
             tma_load_4d_pair(dst + 2 * TILE_A + TILE_B, &p.b_lo, full_c, kc, bn, bi, bo);
           } else {
             mbar_expect_tx(full, STAGE_BYTES);
-            tma_load_4d(dst, &p.a_hi, full, kc, am, bi, bo);
-            tma_load_4d(dst + TILE_A, &p.a_lo, full, kc, am, bi, bo);
+            if (p.conv) {
+              tma_load_im2col(dst, &p.a_hi, full, cx, cw, ch, cn, okw, okh);
+              tma_load_im2col(dst + TILE_A, &p.a_lo, full, cx, cw, ch, cn, okw, okh);
+            } else {
+              tma_load_4d(dst, &p.a_hi, full, kc, am, bi, bo);
+              tma_load_4d(dst + TILE_A, &p.a_lo, full, kc, am, bi, bo);
+            }
             tma_load_4d(dst + 2 * TILE_A, &p.b_hi, full, kc, bn, bi, bo);
             tma_load_4d(dst + 2 * TILE_A + TILE_B, &p.b_lo, full, kc, bn, bi, bo);
           }
@@ -913,7 +942,7 @@ size_t tc_workspace_bytes(const silcu_gemm_args &a) {
   return bytes + partial_bytes(a, tc_plan(a));
 }
 
-silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t s) {
+silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t s, const TcConv *conv) {
   const int64_t Kp = padded_k(a.K > 0 ? a.K : 1);
   const size_t need = tc_workspace_bytes(a);
   if (need > 256 && (!ws || wsb < need))
@@ -948,7 +977,22 @@ silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t
   memset(&p, 0, sizeof(p));
   int launches = 0;
   // A as rows m, K-major.
-  if (asplit) {
+  if (conv) {
+    if (!asplit || a.batch != 1 || bin != 1 || conv->C % BK != 0 || a.M != conv->N * conv->H * conv->W ||
+        a.K != conv->Kf * conv->Kf * conv->C)
+      return fail(SILCU_INVALID_ARGUMENT, "sgemm(tc): convolution operand does not match the GEMM");
+    if (!make_im2col_map(&p.a_hi, conv->in_hi, conv->N, conv->H, conv->W, conv->C, int(conv->pad), BK, BM,
+                         CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_im2col_map(&p.a_lo, conv->in_lo, conv->N, conv->H, conv->W, conv->C, int(conv->pad), BK, BM,
+                         CU_TENSOR_MAP_SWIZZLE_64B))
+      return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeIm2col failed (A)");
+    p.conv = 1;
+    p.cv_H = int(conv->H);
+    p.cv_W = int(conv->W);
+    p.cv_C = int(conv->C);
+    p.cv_K = int(conv->Kf);
+    p.cv_pad = int(conv->pad);
+  } else if (asplit) {
     if (!make_map4(&p.a_hi, a.A_hi, a.K, a.M, a.lda, bin, a.stride_a_inner, bout, a.stride_a, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B) ||
         !make_map4(&p.a_lo, a.A_lo, a.K, a.M, a.lda, bin, a.stride_a_inner, bout, a.stride_a, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B))
       return fail(SILCU_CUDA_ERROR, "sgemm(tc): cuTensorMapEncodeTiled failed (A)");

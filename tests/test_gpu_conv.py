@@ -1,4 +1,5 @@
-"""conv2d (silcu_conv2d_f32: implicit GEMM on the 3xTF32 tensor-core path)
+"""conv2d (silcu_conv2d_f32: GEMM on the 3xTF32 tensor-core path, its A tiles
+im2col TMA boxes of the split input when C_in % 16 == 0, else a split patch matrix)
 against the oracle restatement of the reference's conv2d arithmetic
 (oracle.c: orc_conv2d_f32; the reference has no CPU conv2d) and, for odd
 kernels, an fp64 torch convolution as an independent check.  NHWC input,
@@ -29,6 +30,11 @@ def _torch_ref(x, w):
     (2, 16, 32, 10, 12, 1),  # K = 1 (a per-pixel GEMM)
     (2, 16, 32, 10, 12, 2),  # even K: padding 1 before, 0 after
     (16, 64, 128, 56, 56, 3),  # the reference benchmark's ResNet mid layer
+    # C_in % 16 == 0: the im2col TMA path (no patch matrix)
+    (3, 16, 64, 7, 9, 3),    # M = 189: a partial row tile, tiles that span images
+    (2, 32, 256, 12, 10, 5),  # K = 5 (padding 2), 256-column tiles
+    (1, 128, 64, 16, 16, 3),  # M = 256, K_dim = 1152: split K
+    (2, 48, 36, 11, 13, 4),  # even K = 4 (padding 2 before, 1 after), C_out % 32 != 0
 ])
 def test_conv2d_matches_oracle(cuda, N, C_in, C_out, H, W, K):
     rng = np.random.default_rng(N * 1000 + C_in * 10 + K)
