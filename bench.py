@@ -43,7 +43,7 @@ def parse():
     ap.add_argument("--no-suite", action="store_true", help="skip the per-configuration suite in the headline line")
     ap.add_argument("--suite", action="store_true",
                     help="measure every configuration of the metric (one JSON line each) instead of the headline")
-    ap.add_argument("--profile-case", default=None, choices=["gemm", "block", "shard", "attention", "hbm", "sgemm"],
+    ap.add_argument("--profile-case", default=None, choices=["gemm", "block", "shard", "attention", "hbm", "sgemm", "conv"],
                     help="run only a small case for ncu: the FFN-up GEMM of the workload, a 2-sequence block, "
                          "or the 8-GPU per-rank forward (4 sequences)")
     return ap.parse_args()
@@ -69,6 +69,7 @@ def profile_case(args):
     dominant kernel as the forward does (FFN-up, M=16384 N=3072 K=768, ~600 MB
     on the device) warmup+1 times; `block` runs a 2-sequence transformer forward;
     `shard` the 8-GPU per-rank forward (4 sequences, ~200 MB);
+    `conv` the ResNet mid-layer conv2d of the suite (16x56x56x64 k3 -> 128);
     `attention` the fused attention on a quarter of the BMM-attention config;
     `hbm` the HBM-bound kernels of the suite once each after the warm-ups
     (GEMV 1x4096.4096x4096, small batch 32x4096.4096x768, softmax /
@@ -91,6 +92,12 @@ def profile_case(args):
         for _ in range(args.warmup + 1):
             gpu.attention(qs, ks, vt, Sq=S, Sk=S, batch=BH, heads=1, ldq=d, sq_b=S * d, sq_h=S * d, ldk=d,
                           sk_b=S * d, sk_h=S * d, ldv=S, sv_b=d * S, sv_h=d * S, scale=0.125, O=Ob)
+    elif args.profile_case == "conv":
+        g = torch.Generator(device=dev).manual_seed(0)
+        x = torch.randn(16, 56, 56, 64, device=dev, generator=g)
+        w = torch.randn(128, 3, 3, 64, device=dev, generator=g) * 0.05
+        for _ in range(args.warmup + 1):
+            gpu.conv2d(x, w)
     elif args.profile_case == "sgemm":
         n = 8192  # the metric's SGEMM, plain fp32 operands (split pre-pass + tc_gemm), ~1 GB on the device
         g = torch.Generator(device=dev).manual_seed(0)

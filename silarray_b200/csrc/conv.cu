@@ -46,7 +46,7 @@ bool conv_tc(const ConvShape &s) { return s.C_out % 4 == 0 && s.M >= 64 && s.C_o
 // and the GEMM's A tiles are im2col TMA boxes of it, 16 channels of one
 // filter tap per K block, so C_in must be a multiple of 16.
 bool conv_implicit(const ConvShape &s) {
-  return s.C % 16 == 0 && s.C_out % 4 == 0 && s.M >= 128 && s.C_out >= 32 && s.M * s.C <= int64_t(65535) * 32 * 4096;
+  return s.C % 16 == 0 && s.C_out % 4 == 0 && s.M >= 128 && s.C_out >= 32;
 }
 
 size_t conv_split_bytes(const ConvShape &s) { return (size_t(2) * s.M * s.C * sizeof(float) + 255) / 256 * 256; }
@@ -176,7 +176,7 @@ silcu_status silcu_conv2d_f32(const float *input, const float *weight, float *ou
     uint8_t *w8 = static_cast<uint8_t *>(ws);
     float *hi = reinterpret_cast<float *>(w8);
     float *lo = hi + s.M * s.C;
-    silcu_status r = silcu_split_f32(input, size_t(s.M), size_t(s.C), size_t(s.C), 0, hi, lo, stream);
+    silcu_status r = split_contiguous(input, uint64_t(s.M * s.C), hi, lo, st);  // [M, C] rows, C % 16 == 0
     if (r != SILCU_OK) return r;
     silcu_gemm_args a = conv_gemm_args(s, weight, output);
     a.A_hi = hi;

@@ -38,6 +38,8 @@ struct TcConv {
   const float *in_hi, *in_lo;
   int64_t N, H, W, C, Kf, pad;
 };
+// Exact tf32 split of n contiguous floats (n % 4 == 0, 16-byte aligned).
+silcu_status split_contiguous(const float *src, uint64_t n, float *hi, float *lo, cudaStream_t s);
 silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t ws_bytes, cudaStream_t s,
                     const TcConv *conv = nullptr);
 // The 3xTF32 path's tiling and split-K choice for these arguments.

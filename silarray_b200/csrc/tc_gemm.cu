@@ -942,6 +942,14 @@ size_t tc_workspace_bytes(const silcu_gemm_args &a) {
   return bytes + partial_bytes(a, tc_plan(a));
 }
 
+silcu_status split_contiguous(const float *src, uint64_t n, float *hi, float *lo, cudaStream_t s) {
+  if (n == 0) return SILCU_OK;
+  const uint64_t g = (n / 4 + 255) / 256;
+  const uint64_t cap = uint64_t(sm_count()) * 8;
+  split_contig<<<uint32_t(g < cap ? (g ? g : 1) : cap), 256, 0, s>>>(src, n, hi, lo);
+  return check_launch("split");
+}
+
 silcu_status tc_run(const silcu_gemm_args &a, void *ws, size_t wsb, cudaStream_t s, const TcConv *conv) {
   const int64_t Kp = padded_k(a.K > 0 ? a.K : 1);
   const size_t need = tc_workspace_bytes(a);
