@@ -114,6 +114,50 @@ def test_attention_split_kv(cuda, monkeypatch, splits, B, H, Sq, Sk):
     gpu.device_status()
 
 
+@pytest.mark.parametrize("splits", [2, 3])
+def test_attention_split_kv_vt(cuda, monkeypatch, splits):
+    """Split-KV with V given as V^T (K-major) and Sq != Sk, ragged: within the
+    oracle chain's tolerance, and a workspace smaller than the split needs
+    runs the call unsplit (the same result as one range, bit for bit)."""
+    import ctypes as ct
+    from silarray_b200 import _lib
+    B, H, Sq, Sk, D = 1, 2, 150, 900, 64
+    q, k, v = _attn_inputs(B, H, Sq, Sk, 77 + splits)
+    dq, dk, dv = (torch.from_numpy(t).cuda().reshape(-1) for t in (q, k, v))
+    qs = gpu.split(dq, B * H * Sq, D)
+    ks = gpu.split(dk, B * H * Sk, D)
+    vt = gpu.transpose_split(dv, Sk, D, D, batch=B, heads=H, s_b=H * Sk * D, s_h=Sk * D)
+    common = dict(Sq=Sq, Sk=Sk, batch=B, heads=H, ldq=D, sq_b=H * Sq * D, sq_h=Sq * D, ldk=D, sk_b=H * Sk * D,
+                  sk_h=Sk * D, scale=float(np.float32(0.125)), ldv=Sk, sv_b=H * D * Sk, sv_h=D * Sk)
+    monkeypatch.setenv("SILCU_ATTN_SPLITS", str(splits))
+    got = gpu.attention(qs, ks, vt, **common)
+    torch.cuda.synchronize()
+    g = got.cpu().numpy().reshape(B, H, Sq, D)
+    for h in range(H):
+        assert_dot_close(g[0, h], _ref(q[0, h], k[0, h], v[0, h], np.float32(0.125)), Sk,
+                         what=f"split {splits} attention (V^T) h{h}")
+    # the same arguments through silcu_attention_ex with no workspace: unsplit
+    a = _lib.AttnArgs()
+    a.Q_hi, a.Q_lo = qs[0].data_ptr(), qs[1].data_ptr()
+    a.K_hi, a.K_lo = ks[0].data_ptr(), ks[1].data_ptr()
+    a.Vt_hi, a.Vt_lo = vt[0].data_ptr(), vt[1].data_ptr()
+    o2 = torch.empty(B * H * Sq * D, device="cuda")
+    a.O = o2.data_ptr()
+    a.Sq, a.Sk, a.D, a.batch, a.heads = Sq, Sk, D, B, H
+    a.ldq, a.sq_b, a.sq_h = D, H * Sq * D, Sq * D
+    a.ldk, a.sk_b, a.sk_h = D, H * Sk * D, Sk * D
+    a.ldv, a.sv_b, a.sv_h = Sk, H * D * Sk, D * Sk
+    a.ldo, a.so_b, a.so_h = D, H * Sq * D, Sq * D
+    a.scale = float(np.float32(0.125))
+    assert gpu.lib().silcu_attention_workspace_bytes(ct.byref(a)) > 0
+    _lib.check(gpu.lib().silcu_attention_ex(ct.byref(a), None, 0, gpu._stream()))
+    monkeypatch.setenv("SILCU_ATTN_SPLITS", "1")
+    o1 = gpu.attention(qs, ks, vt, **common)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(o2.cpu().numpy(), o1.cpu().numpy())
+    gpu.device_status()
+
+
 def test_attention_split_choice(cuda, monkeypatch):
     """The split is taken by shape: one query tile over 4096 keys splits (a
     workspace is asked for); the benchmark's 12 heads x 4 query tiles x batch
