@@ -1107,12 +1107,79 @@ __global__ void __launch_bounds__(128) sum_axis_seq_kernel(const float *__restri
   }
 }
 
+// Rows (inner == 1, len % 4 == 0, 16-byte aligned): one warp per 32 rows,
+// lane r adding row r in column order -- the sequential sum, bit for bit --
+// from shared memory, where the warp stages 32 x 32 tiles with coalesced
+// 16-byte cp.async copies (4 rows x 128 B per instruction) through an
+// 8-stage ring, so the loads of later tiles are in flight while the adds of
+// the current one run (16 stages, 72 KB: one warp per SM streams a row
+// block, so the ring depth sets the bytes in flight).  Rows padded to 36
+// floats (16-byte aligned copies).
+constexpr int kSeqTile = 32, kSeqStages = 16, kSeqPad = kSeqTile + 4;
+constexpr int kSeqSmem = kSeqStages * 32 * kSeqPad * 4;
+
+__global__ void __launch_bounds__(32) sum_rows_seq_kernel(const float *__restrict__ in, float *__restrict__ out,
+                                                          uint64_t rows, uint64_t len) {
+  extern __shared__ __align__(16) float seq_smem[];
+  float(*buf)[32][kSeqPad] = reinterpret_cast<float(*)[32][kSeqPad]>(seq_smem);
+  const int lane = threadIdx.x;
+  const uint64_t r0 = uint64_t(blockIdx.x) * 32;
+  const uint64_t ntiles = (len + kSeqTile - 1) / kSeqTile;
+  auto issue = [&](uint64_t t) {
+    if (t < ntiles) {
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const int row = i * 4 + (lane >> 3), chunk = lane & 7;
+        const uint64_t col = t * kSeqTile + uint64_t(chunk) * 4;
+        if (r0 + row < rows && col < len) {
+          const float *src = in + (r0 + row) * len + col;
+          const uint32_t dst = uint32_t(__cvta_generic_to_shared(&buf[t % kSeqStages][row][chunk * 4]));
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+        }
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+#pragma unroll 1
+  for (int t = 0; t < kSeqStages - 1; t++) issue(uint64_t(t));
+  float s = 0.0f;
+#pragma unroll 1
+  for (uint64_t t = 0; t < ntiles; t++) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kSeqStages - 2) : "memory");
+    __syncwarp();
+    const float *row = buf[t % kSeqStages][lane];
+    const uint64_t n = len - t * kSeqTile < uint64_t(kSeqTile) ? len - t * kSeqTile : uint64_t(kSeqTile);
+    if (n == kSeqTile) {
+#pragma unroll
+      for (int c = 0; c < kSeqTile; c++) s = __fadd_rn(s, row[c]);
+    } else {
+      for (uint64_t c = 0; c < n; c++) s = __fadd_rn(s, row[c]);
+    }
+    __syncwarp();  // every lane is done with this stage before it is refilled
+    issue(t + kSeqStages - 1);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  if (r0 + lane < rows) out[r0 + lane] = s;
+}
+
 silcu_status silcu_sum_axis_seq_f32(const float *in, float *out, size_t outer, size_t len, size_t inner,
                                     silcu_stream stream) {
   const size_t total = outer * inner;
   if (total == 0) return SILCU_OK;
   if (!in || !out) return fail(SILCU_INVALID_ARGUMENT, "sum_axis_seq: null pointer");
   const int vec = inner == 1 && len % 4 == 0 && aligned16(in) ? 1 : 0;
+  if (vec && len > 0 && (outer + 31) / 32 <= 0x7FFFFFFFull) {
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(sum_rows_seq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSeqSmem);
+      if (e != cudaSuccess) return fail(SILCU_CUDA_ERROR, "sum_axis_seq: smem attribute: %s", cudaGetErrorString(e));
+      configured[dev] = true;
+    }
+    sum_rows_seq_kernel<<<unsigned((outer + 31) / 32), 32, kSeqSmem, as_stream(stream)>>>(in, out, outer, len);
+    return check_launch("sum_axis_seq");
+  }
   uint64_t grid = (total + 127) / 128;
   const uint64_t cap = uint64_t(sm_count()) * 16;
   if (grid > cap) grid = cap;

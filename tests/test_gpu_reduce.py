@@ -180,7 +180,10 @@ def test_small_sum_is_sequential_fp32(cuda, n):
 
 
 @pytest.mark.parametrize("shape,axis", [((7, 300, 33), 0), ((7, 300, 33), 1), ((7, 300, 33), 2),
-                                        ((4096, 1024), 1), ((3, 5), 1), ((2, 1001), 1)])
+                                        ((4096, 1024), 1), ((3, 5), 1), ((2, 1001), 1),
+                                        # rows through the warp-per-32-rows kernel: a partial
+                                        # warp of rows, a partial last tile, one short tile
+                                        ((33, 36), 1), ((100, 8192), 1), ((5, 4), 1), ((70, 1000), 1)])
 def test_sum_axis_sequential_bit_exact(cuda, shape, axis):
     """silcu_sum_axis_seq_f32 adds in the reference CPU loop's order
     (include/array.h:2303-2317): bit-identical to the oracle's restatement."""
