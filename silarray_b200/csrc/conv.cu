@@ -172,7 +172,14 @@ silcu_status silcu_conv2d_f32(const float *input, const float *weight, float *ou
   const size_t need = silcu_conv2d_workspace_bytes(N, H, W, C_in, K, C_out);
   if (!ws || wsb < need) return fail(SILCU_WORKSPACE_TOO_SMALL, "conv2d: workspace %zu < %zu", wsb, need);
   cudaStream_t st = as_stream(stream);
-  if (conv_implicit(s) && aligned16(input) && aligned16(output) && aligned16(weight) && s.Kd % 4 == 0) {
+  // the implicit path when the driver accepts the im2col map for this shape
+  // (checked on a dummy encode; the patch-matrix path otherwise)
+  CUtensorMap probe;
+  const bool im2col_ok = conv_implicit(s) && aligned16(input) && aligned16(output) && aligned16(weight) &&
+                         s.Kd % 4 == 0 &&
+                         make_im2col_map(&probe, input, s.N, s.H, s.W, s.C, int(s.pad), 16, 128,
+                                         CU_TENSOR_MAP_SWIZZLE_64B);
+  if (im2col_ok) {
     uint8_t *w8 = static_cast<uint8_t *>(ws);
     float *hi = reinterpret_cast<float *>(w8);
     float *lo = hi + s.M * s.C;
