@@ -177,7 +177,7 @@ silcu_status silcu_conv2d_f32(const float *input, const float *weight, float *ou
   CUtensorMap probe;
   const bool im2col_ok = conv_implicit(s) && aligned16(input) && aligned16(output) && aligned16(weight) &&
                          s.Kd % 4 == 0 &&
-                         make_im2col_map(&probe, input, s.N, s.H, s.W, s.C, int(s.pad), 16, 128,
+                         tc::make_im2col_map(&probe, input, s.N, s.H, s.W, s.C, int(s.pad), 16, 128,
                                          CU_TENSOR_MAP_SWIZZLE_64B);
   if (im2col_ok) {
     uint8_t *w8 = static_cast<uint8_t *>(ws);
