@@ -170,6 +170,14 @@ __device__ __forceinline__ float exp_ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(__fmul_rn(x, kLog2e)));
   return y;
 }
+// 2^(x log2 e - mlog2) for x <= the max whose product with log2 e is mlog2
+// (x = -inf gives 0; the fused product-difference differs from rounding
+// (x - max) first by at most |max log2 e| 2^-24 in the exponent).
+__device__ __forceinline__ float ex2_fma(float x, float mlog2) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(__fmaf_rn(x, kLog2e, -mlog2)));
+  return y;
+}
 
 // TMEM load of N (16 or 32, or 64 as two 32s) consecutive columns of this warp's lanes.
 __device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t *r) {
@@ -467,10 +475,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
 #pragma unroll
       for (int e = 0; e < ESPLIT; e++) m_new = fmaxf(m_new, xmax[e * QT + r]);
       const float corr = (m == m_new) ? 1.0f : exp_ex2(__fsub_rn(m, m_new));
+      // e^(x - m) = 2^(x log2 e - m log2 e): one fused multiply-add per score
+      // (the max's product rounded once per block, -inf for an empty row)
+      const float mlog2 = __fmul_rn(m_new, kLog2e);
       float ps = 0.0f;
 #pragma unroll
       for (int i = 0; i < HK; i++) {
-        const float e = exp_ex2(__fsub_rn(sc[i], m_new));
+        const float e = ex2_fma(sc[i], mlog2);
         sc[i] = e;
         ps += e;
       }
