@@ -29,6 +29,7 @@
 // Shared memory: Q 64 KB + K 64 KB + V 64 KB = 192 KB.  TMEM (512 columns):
 // S / P_hi 2 x 128, P_lo 128, O 2 x 64.
 // All waits are bounded (as in tc_gemm.cu); no TMA multicast, no clusters.
+#include <cmath>
 #include <stdlib.h>
 #include <string.h>
 
@@ -74,6 +75,11 @@ struct __align__(64) AttnParams {
   int Sq, Sk, heads, tiles_q;
   int v_rows;  // V given as [Sk, D] rows (B operand of P.V read MN-major), else V^T [D, Sk]
   float scale;
+  // scale_pow2: scale is a positive power of two, so fl(s * scale) is exact
+  // and folds into the exponent (scale_log2e = scale * log2 e, also exact)
+  // and into the block max (max fl(s * scale) = fl(max s * scale)).
+  int scale_pow2;
+  float scale_log2e;
   int *err;
   // Split KV: the key blocks of each (batch, head, query tile) in kv_splits
   // contiguous ranges, one CTA each; with kv_splits > 1 a CTA writes its
@@ -170,12 +176,12 @@ __device__ __forceinline__ float exp_ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(__fmul_rn(x, kLog2e)));
   return y;
 }
-// 2^(x log2 e - mlog2) for x <= the max whose product with log2 e is mlog2
-// (x = -inf gives 0; the fused product-difference differs from rounding
-// (x - max) first by at most |max log2 e| 2^-24 in the exponent).
-__device__ __forceinline__ float ex2_fma(float x, float mlog2) {
+// 2^(x c - mlog2): with c = log2 e and mlog2 = max log2 e it is e^(x - max)
+// for x <= max (x = -inf gives 0; the fused product-difference differs from
+// rounding (x - max) first by at most |max log2 e| 2^-24 in the exponent).
+__device__ __forceinline__ float ex2_fma(float x, float c, float mlog2) {
   float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(__fmaf_rn(x, kLog2e, -mlog2)));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(__fmaf_rn(x, c, -mlog2)));
   return y;
 }
 
@@ -201,6 +207,7 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]) {
 
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+template <bool POW2>
 __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw);
@@ -464,11 +471,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
       const bool tail = key0 + KB > p.Sk;
 #pragma unroll
       for (int i = 0; i < HK; i++) {
-        float x = __fmul_rn(sc[i], p.scale);           // the reference's `* scale` node
+        // the reference's `* scale` node (exact, and applied below, for a power-of-two scale)
+        float x = POW2 ? sc[i] : __fmul_rn(sc[i], p.scale);
         if (tail && key0 + HK * hh + i >= p.Sk) x = __int_as_float(0xff800000);
         sc[i] = x;
         mj = fmaxf(mj, x);
       }
+      if (POW2) mj = __fmul_rn(mj, p.scale);
       xmax[hh * QT + r] = mj;
       asm volatile("bar.sync 1, %0;" ::"n"(32 * EPI_WARPS) : "memory");
       float m_new = m;
@@ -481,7 +490,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_kernel(const __grid_const
       float ps = 0.0f;
 #pragma unroll
       for (int i = 0; i < HK; i++) {
-        const float e = ex2_fma(sc[i], mlog2);
+        const float e = ex2_fma(sc[i], POW2 ? p.scale_log2e : kLog2e, mlog2);
         sc[i] = e;
         ps += e;
       }
@@ -673,13 +682,21 @@ silcu_status attention_launch(const silcu_attention_args *ap, int64_t S, void *w
   p.heads = int(a.heads);
   p.tiles_q = int(tiles_q);
   p.scale = a.scale;
+  {
+    int ex = 0;
+    const bool normal = std::isfinite(a.scale) && a.scale > 0.0f && std::fabs(a.scale) >= 1.17549435e-38f;
+    p.scale_pow2 = (normal && std::frexp(a.scale, &ex) == 0.5f && ex > -100 && ex < 100) ? 1 : 0;
+    p.scale_log2e = a.scale * kLog2e;
+  }
   p.err = device_error_ptr();
   if (!p.err) return fail(SILCU_CUDA_ERROR, "attention: no device error word");
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return fail(SILCU_CUDA_ERROR, "attention: smem attribute: %s", cudaGetErrorString(e));
     configured[dev] = true;
   }
@@ -698,7 +715,10 @@ silcu_status attention_launch(const silcu_attention_args *ap, int64_t S, void *w
   }
   // persistent: one CTA per SM, items dealt round-robin
   const int64_t grid = U * S < sm_count() ? U * S : sm_count();
-  attn_kernel<<<uint32_t(grid), NUM_THREADS, SMEM_BYTES, as_stream(stream)>>>(p);
+  if (p.scale_pow2)
+    attn_kernel<true><<<uint32_t(grid), NUM_THREADS, SMEM_BYTES, as_stream(stream)>>>(p);
+  else
+    attn_kernel<false><<<uint32_t(grid), NUM_THREADS, SMEM_BYTES, as_stream(stream)>>>(p);
   silcu_status r = check_launch("attention");
   if (r != SILCU_OK || S == 1) return r;
   const int64_t threads = U * QT * (HD / 4);
